@@ -1,0 +1,337 @@
+"""Benchmark of the b200_fp8 VC-Attention forward (configuration 3).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one full forward of the hot path over one batch on each GPU:
+Lloyd clustering of V (a refresh step), Q/K demean + Hadamard + E4M3 block
+quantisation, V tiles, and the fused tcgen05 attention; B=1, H=40, S=32768,
+D=128, bf16 inputs, combined mode (ExpCast + V-Smooth), step 0 of 50.  With
+N GPUs (torchrun) every rank runs its own batch (weak scaling; global batch
+N), heads are independent so no collective touches the data path.
+
+value     FP8 attention TFLOPS, 4*B*H*S^2*D per step, summed over ranks, from
+          CUDA-event time of the step with inputs resident in HBM (max over
+          ranks).  Q/K/V (1 GB) exceed the 126 MB L2, so no flush is needed.
+e2e       the same metric through the public API (vc_attention_b200.attention)
+          with a pinned host->device copy of Q/K/V and a device->host copy of
+          the output inside every timed step.
+roofline  the fused attention kernel alone, timed with CUDA events on its
+          stream, against the FP8 dense tensor peak measured in the same run
+          (torch._scaled_mm, 8192^3, E4M3 -> BF16).
+cpu_baseline / --impl reference
+          the CPU restatement of the reference backend (oracle/) on the host
+          cores, on a bounded sample (one head, 8 query tiles over all keys,
+          with that head's full preprocessing), scaled to TFLOPS.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "vc-attention_b200"))
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+B, H, S, D = 1, 40, 32768, 128
+METRIC = "FP8 attn fwd TFLOPS/GPU (4*B*H*S^2*D/t) at S=32k; % of FP8 MMA peak"
+UNIT = "TFLOPS"
+LAUNCHES_PER_STEP = 13   # clustering 7 (init, 2 x (assign, update), offsets, scatter), Q/K 4, V 1, attention 1
+CONFIG = {"workload": "c3: B1 H40 S32768 D128 bf16 combined (ExpCast + V-Smooth), refresh step 0/50",
+          "global_batch": None, "seq_len": S, "heads": H, "head_dim": D, "parallelism": None,
+          "l2": "inputs (1 GB Q/K/V per GPU) larger than L2; no flush"}
+
+
+def flops(b=B, h=H, sq=S, sk=S, d=D):
+    return 4.0 * b * h * sq * sk * d
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        torch.distributed.barrier()
+
+
+class Clocks:
+    """Samples SM clocks and throttle reasons with nvidia-smi during a region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            self.proc.wait(timeout=10)
+
+    def summary(self):
+        rows = []
+        try:
+            for line in open(self.path):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        except OSError:
+            pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def fp8_peak_tflops(device):
+    """Dense E4M3 GEMM throughput of this GPU (cuBLAS via torch._scaled_mm)."""
+    n = 8192
+    a = torch.randn(n, n, device=device).to(torch.float8_e4m3fn)
+    b = torch.randn(n, n, device=device).to(torch.float8_e4m3fn).t()
+    one = torch.ones((), device=device)
+    for _ in range(3):
+        torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+    best = float("inf")
+    for _ in range(5):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(10):
+            torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+        e.record()
+        e.synchronize()
+        best = min(best, s.elapsed_time(e) / 10)
+    return 2 * n ** 3 / (best * 1e-3) / 1e12
+
+
+def cpu_reference(threads, heads=1, q_tiles=32):
+    """Times the CPU restatement of the reference backend on one head: the
+    full O(S) preprocessing (Lloyd, Q/K quantisation, V tiles) plus the
+    streaming attention of `q_tiles` 128-row query tiles over all S keys."""
+    import numpy as np
+    from threadpoolctl import threadpool_limits
+
+    from oracle import oracle as O
+    from vc_attention_b200.synthetic import make_qkv
+
+    q, k, v = make_qkv("c3", 1234, heads=heads)
+    flat = [x.float().reshape(heads, S, D).numpy() for x in (q, k, v)]
+    rows = q_tiles * 128
+    t0 = time.perf_counter()
+    with threadpool_limits(limits=1):
+        pi, _, _ = O.group_values(flat[2], clusters=8, iterations=2)
+        prep = O.Prepared(flat[0][:, :rows], flat[1], flat[2], pi=pi, active=True, q_block=128,
+                          k_quant_block=256, kv_block=128, mean_dtype="float16", k_smooth=True, qk_hadamard=True)
+        from concurrent.futures import ThreadPoolExecutor
+        chunks = [slice(r, r + 128) for r in range(0, rows, 128)]
+        with ThreadPoolExecutor(max_workers=threads) as pool:
+            outs = list(pool.map(lambda sl: O.stream(prep, sl, expcast=True, scale=D ** -0.5), chunks))
+    dt = time.perf_counter() - t0
+    assert all(np.isfinite(o).all() for o in outs)
+    sample_flops = flops(1, heads, rows, S, D)
+    return {"value": sample_flops / dt / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{heads} head(s), {q_tiles} query tiles x {S} keys, with the head's full clustering, "
+                      f"Q/K and V preprocessing; {dt:.2f} s"}
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    threads = len(os.sched_getaffinity(0))
+    times = []
+    for i in range(args.warmup + args.steps):
+        r = cpu_reference(threads)
+        if i >= args.warmup:
+            times.append(r)
+    value = statistics.median(x["value"] for x in times)
+    cpu = dict(times[0])
+    cpu["value"] = value
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": flops(1, 1, 32 * 128, S, D) / value / 1e9,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": dict(CONFIG, global_batch=1, parallelism="cpu"), "cpu_baseline": cpu,
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+
+
+def run_ours(args, world, rank, local):
+    from vc_attention_b200 import Config, LayoutCache, attention, stages
+    from vc_attention_b200.b200_backend import forward, group_values
+    from vc_attention_b200.synthetic import make_qkv
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    cfg = Config(v_smooth=True, expcast=True)
+    q, k, v = make_qkv("c3", 1000 + rank, device=device)
+    scale = D ** -0.5
+    out = torch.empty_like(q)
+    status = torch.zeros(1, dtype=torch.int32, device=device)
+    workspace = None
+
+    def step():
+        nonlocal workspace
+        pi, _ = group_values(v, clusters=cfg.clusters, iterations=cfg.iterations)
+        if workspace is None:
+            import ctypes
+            from vc_attention_b200 import _abi
+            from vc_attention_b200.b200_backend import forward_args, _extension
+            need = _extension().vcb_forward_workspace(ctypes.byref(forward_args(q, k, v, cfg, pi, True, scale, out)))
+            workspace = torch.empty(need, dtype=torch.uint8, device=device)
+        forward(q, k, v, cfg, pi=pi, active=True, scale=scale, out=out, workspace=workspace, status=status,
+                check_status=False)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with Clocks(local) as clocks:
+        torch.cuda.synchronize()
+        barrier(world)
+        for s, e in ev:
+            s.record()
+            step()
+            e.record()
+        torch.cuda.synchronize()
+    barrier(world)
+    ms = sum(s.elapsed_time(e) for s, e in ev) / args.steps
+    if int(status.item()) != 0:
+        raise RuntimeError(f"device status flags {int(status.item())}")
+    ms_max = max_over_ranks(ms, world)
+    value = world * flops() / (ms_max * 1e-3) / 1e12
+
+    # dominant kernel alone: the fused attention on prepared operands
+    pi, _ = group_values(v, clusters=8, iterations=2)
+    q8, qs, k8, ks = stages.quantize_qk(q, k, pi=pi)
+    v8, meta = stages.prepare_v(v, pi=pi, active=True)
+    attn_out = torch.empty((H, S, D), dtype=torch.bfloat16, device=device)
+
+    def attn():
+        stages.attention_fp8(q8, qs, k8, ks, v8, meta, heads=H, sq=S, sk=S, dv=D, expcast=True, has_mean=True,
+                             scale=scale, out=attn_out)
+
+    for _ in range(3):
+        attn()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = max(3, args.steps)
+    s.record()
+    for _ in range(reps):
+        attn()
+    e.record()
+    e.synchronize()
+    attn_ms = s.elapsed_time(e) / reps
+    attn_ms = max_over_ranks(attn_ms, world)
+    achieved = flops() / (attn_ms * 1e-3) / 1e12
+    peak = fp8_peak_tflops(device)
+    traffic = None
+    tfile = ROOT / "profiles" / "attn_kernel_traffic.json"
+    if tfile.exists():
+        traffic = json.loads(tfile.read_text()).get("bytes_per_launch_full_c3")
+
+    # end to end through the public API, host buffers in and out
+    hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
+    hout = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    barrier(world)
+    e2e_ms = []
+    for i in range(args.warmup + args.steps):
+        torch.cuda.synchronize()
+        barrier(world)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        dq, dk, dv = (x.to(device, non_blocking=True) for x in (hq, hk, hv))
+        res, _ = attention(dq, dk, dv, cfg, cache=LayoutCache(cfg), step=0, total_steps=50, request_id=i)
+        hout.copy_(res, non_blocking=True)
+        e.record()
+        e.synchronize()
+        if i >= args.warmup:
+            e2e_ms.append(s.elapsed_time(e))
+    e2e = max_over_ranks(sum(e2e_ms) / len(e2e_ms), world)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_reference(len(os.sched_getaffinity(0)))
+    if rank == 0:
+        nbytes = q.numel() * q.element_size()
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "e4m3 (bf16 in/out, fp32 accumulate)", "data": "synthetic",
+            "config": dict(CONFIG, global_batch=world, parallelism=f"heads independent, {world} rank(s)"),
+            "e2e": {"value": world * flops() / (e2e * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": e2e,
+                    "h2d_bytes_per_step": 3 * nbytes, "d2h_bytes_per_step": nbytes},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": traffic, "kernel": "attn_kernel",
+                         "kernel_ms": attn_ms,
+                         "peak_source": "measured in this run: torch._scaled_mm E4M3 8192^3 burst",
+                         "frac_of_spec_4500": achieved / 4500.0},
+            "cpu_baseline": cpu,
+            "clocks": clocks.summary(),
+            "gpu_launches": LAUNCHES_PER_STEP * args.steps,
+        }
+        print(json.dumps(line))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    world, rank, local = dist_setup()
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank)
+        else:
+            run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,191 @@
+/*
+ * vcb.h - C ABI of the B200 (sm_100a) VC-Attention forward path.
+ *
+ * This library replaces the pybind11 extension of czfsdg/vc-attention
+ * (csrc/bindings.cpp, PYBIND11_MODULE at bindings.cpp:231-248) with plain C
+ * entry points: pointers, sizes and a CUDA stream, no torch types.  Every
+ * buffer (inputs, outputs, scratch) belongs to the caller; the library
+ * allocates no device memory and keeps no per-call state.  All work is
+ * enqueued on the stream the caller passes (bindings.cpp:176 uses the
+ * current PyTorch stream the same way); nothing synchronises the device.
+ *
+ * Tensors are contiguous, batch and heads flattened: [heads, tokens, dim].
+ * Functions return VCB_OK or a VCB_ERR_* code; vcb_last_error() gives the
+ * message of the last failure on the calling thread.
+ */
+#ifndef VCB_H
+#define VCB_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define VCB_API __attribute__((visibility("default")))
+#else
+#define VCB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define VCB_ABI_VERSION 1
+#define VCB_NUMERICAL_CONTRACT_VERSION 2   /* bindings.cpp:232 */
+
+enum vcb_status {
+    VCB_OK = 0,
+    VCB_ERR_INVALID_ARGUMENT = 1,   /* shape, geometry, pointer or alignment */
+    VCB_ERR_UNSUPPORTED_DEVICE = 2, /* device is not compute capability 10.0 */
+    VCB_ERR_CUDA = 3,               /* a CUDA runtime or driver call failed */
+    VCB_ERR_WORKSPACE = 4           /* workspace smaller than required */
+};
+
+enum vcb_dtype { VCB_F32 = 0, VCB_F16 = 1, VCB_BF16 = 2 };
+
+/* Bits of the device status word that kernels set (see vcb_read_status). */
+enum vcb_device_flags {
+    VCB_FLAG_NONFINITE = 1,         /* a Q, K or V element was NaN or Inf */
+    VCB_FLAG_TIMEOUT = 2            /* a bounded wait in the attention kernel expired */
+};
+
+/* ---- identification --------------------------------------------------- */
+VCB_API int vcb_abi_version(void);
+/* replaces the module attribute numerical_contract_version (bindings.cpp:232) */
+VCB_API int vcb_numerical_contract_version(void);
+/* replaces build_info() (bindings.cpp:237-247); returns a static JSON string */
+VCB_API const char* vcb_build_info(void);
+/* copies the last error message of this thread into buf; returns its length */
+VCB_API size_t vcb_last_error(char* buf, size_t size);
+/* VCB_OK when `device` is compute capability 10.0 (sm_100), else an error */
+VCB_API int vcb_check_device(int device);
+
+/* ---- ExpCast bytes ------------------------------------------------------ */
+/* replaces expcast_codes(x) (bindings.cpp:219-227; kernel kernels.cu:61-70):
+ * codes[i] = rne(clamp(fmaf(x[i], 11.541560173034668f, 119.6500015258789f), 0, 120)) */
+VCB_API int vcb_expcast_codes(const float* x, uint8_t* codes, int64_t n, void* stream);
+
+/* ---- Q/K preprocessing ---------------------------------------------------- */
+typedef struct {
+    const void* q;          /* [heads, sq, d]  dtype */
+    const void* k;          /* [heads, sk, d]  dtype */
+    int dtype;              /* vcb_dtype */
+    int64_t heads, sq, sk;
+    int d;                  /* 1..128 */
+    const int32_t* pi;      /* [heads, sk] K row permutation, or NULL */
+    int k_smooth;           /* subtract the per-head K channel mean */
+    int hadamard;           /* normalised Sylvester transform, width = next pow2 >= d */
+    /* transform-only outputs (vcb_preprocess_qk): float [heads, s, width] */
+    float* q_out;
+    float* k_out;
+    /* quantised outputs (vcb_quantize_qk) */
+    int q_block, k_quant_block;
+    uint8_t* q8;            /* [heads, sq_pad, 128] e4m3, sq_pad = vcb_padded_rows(sq, q_block) */
+    uint8_t* k8;            /* [heads, sk_pad, 128] e4m3 */
+    float* q_scale;         /* [heads, ceil(sq / q_block)] */
+    float* k_scale;         /* [heads, ceil(sk / k_quant_block)] */
+    int32_t* status;        /* device status word (nullable) */
+    void* workspace;
+    size_t workspace_bytes;
+} vcb_qk_args;
+
+/* rows of a payload buffer: whole quantisation blocks and whole 128-row tiles */
+VCB_API int64_t vcb_padded_rows(int64_t rows, int block);
+VCB_API size_t vcb_qk_workspace(int64_t heads, int64_t sk);
+/* replaces preprocess_qk(q, k, k_smooth, hadamard) (bindings.cpp:68-98):
+ * writes q_out / k_out only */
+VCB_API int vcb_preprocess_qk(const vcb_qk_args* args, void* stream);
+/* demean + Hadamard + block E4M3 quantisation in one pass (replaces
+ * kernels.cu:72-120, launched at kernels.cu:307-310): writes q8/k8/scales */
+VCB_API int vcb_quantize_qk(const vcb_qk_args* args, void* stream);
+
+/* ---- V clustering (Lloyd + stable permutation) ---------------------------- */
+typedef struct {
+    const void* v;          /* [heads, s, d] dtype */
+    int dtype;
+    int64_t heads, s;
+    int d;                  /* 1..128 */
+    int clusters;           /* 1..32; count = min(clusters, s) */
+    int iterations;         /* >= 1 */
+    const float* centers_in;/* [heads, count, d] warm start, or NULL for equispaced init */
+    float* centers_out;     /* [heads, count, d] */
+    int32_t* pi;            /* [heads, s] stable argsort of the final labels */
+    void* workspace;
+    size_t workspace_bytes;
+} vcb_group_args;
+
+VCB_API size_t vcb_group_workspace(int64_t heads, int64_t s, int d, int clusters);
+/* replaces group_values(v, clusters, iterations, centers) (bindings.cpp:182-217) */
+VCB_API int vcb_group_values(const vcb_group_args* args, void* stream);
+
+/* ---- V tiles ------------------------------------------------------------- */
+typedef struct {
+    const void* v;          /* [heads, s, dv] dtype */
+    int dtype;
+    int64_t heads, s;
+    int dv;                 /* 1..128 */
+    const int32_t* pi;      /* [heads, s] or NULL */
+    int active;             /* subtract the block mean (V-Smooth window) */
+    int mean_type;          /* 0 fp32, 1 fp16, 2 bf16 (cuda_backend.py:52 encoding) */
+    int kv_block;           /* 128 */
+    uint8_t* v8;            /* [heads, T, 128 channels, kv_block tokens] e4m3 residual */
+    float* v_meta;          /* [heads, T, 2, 128]: vscale, then mu/vscale at mean_type */
+    int32_t* status;        /* device status word (nullable) */
+} vcb_v_args;
+
+/* replaces prepare_values (kernels.cu:124-162, launch kernels.cu:311-312) and
+ * the V gather of cuda_backend.py:51 */
+VCB_API int vcb_prepare_v(const vcb_v_args* args, void* stream);
+
+/* ---- fused attention over prepared operands ------------------------------- */
+typedef struct {
+    const uint8_t* q8; const float* q_scale;
+    const uint8_t* k8; const float* k_scale;
+    const uint8_t* v8; const float* v_meta;
+    int64_t heads, sq, sk;
+    int dv;
+    int q_block, k_quant_block, kv_block;
+    int expcast;
+    int has_mean;           /* v_meta carries non-zero block means (V-Smooth active) */
+    float scale;            /* softmax scale, positive finite */
+    void* out;              /* [heads, sq, dv] */
+    int out_dtype;          /* vcb_dtype */
+    int32_t* status;        /* device status word (nullable) */
+} vcb_attn_args;
+
+/* replaces the host tile loop of kernels.cu:313-330 (two cuBLASLt FP8 GEMMs
+ * and four SIMT kernels per tile pair) with one warp-specialised tcgen05
+ * kernel: TMA-staged E4M3 tiles, S and PV accumulators in tensor memory,
+ * online softmax with ExpCast and V-mean recovery, output in out_dtype */
+VCB_API int vcb_attention_fp8(const vcb_attn_args* args, void* stream);
+
+/* ---- whole forward ----------------------------------------------------------- */
+typedef struct {
+    const void* q; const void* k; const void* v;
+    int dtype;
+    int64_t heads, sq, sk;
+    int d, dv;
+    const int32_t* pi;      /* [heads, sk] or NULL */
+    int q_block, k_quant_block, kv_block;
+    int smooth;             /* V-Smooth demean active */
+    int expcast;
+    int mean_type;
+    float scale;
+    int k_smooth, hadamard;
+    void* out;              /* [heads, sq, dv] dtype */
+    void* workspace;
+    size_t workspace_bytes;
+    int32_t* status;        /* device status word (nullable); zeroed by the call */
+} vcb_forward_args;
+
+VCB_API size_t vcb_forward_workspace(const vcb_forward_args* args);
+/* replaces forward(q, k, v, bq, k_quant, bk, smooth, expcast, mean_type,
+ * scale, k_smooth, hadamard) (bindings.cpp:100-178) */
+VCB_API int vcb_forward(const vcb_forward_args* args, void* stream);
+
+/* Waits for `stream`, then reads the device status word into *flags. */
+VCB_API int vcb_read_status(const int32_t* status, void* stream, int32_t* flags);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* VCB_H */

@@ -122,11 +122,17 @@ def k_mean(k):
     return out
 
 
-def preprocess_qk(q, k, *, k_smooth, qk_hadamard):
-    """core.py:88-99: demean K over tokens, then rotate Q and K."""
+def preprocess_qk(q, k, *, k_smooth, qk_hadamard, pi=None):
+    """core.py:88-99: demean K over tokens, then rotate Q and K.  With a
+    permutation pi, K rows are gathered (core.py:289) before the demean; the
+    mean itself is summed in original token order (the fixed order of
+    vc_oracle.c), which is the same set of tokens."""
     q, k = _f32(q), _f32(k)
+    mean = k_mean(k)[:, None, :] if k_smooth else None
+    if pi is not None:
+        k = np.take_along_axis(k, np.asarray(pi, dtype=np.int64)[:, :, None], axis=1)
     if k_smooth:
-        k = k - k_mean(k)[:, None, :]
+        k = k - mean
     if qk_hadamard:
         q, k = hadamard(q), hadamard(k)
     return q, k
@@ -207,11 +213,8 @@ class Prepared:
     def __init__(self, q, k, v, *, pi, active, q_block, k_quant_block, kv_block, mean_dtype,
                  k_smooth, qk_hadamard):
         q, k, v = _f32(q), _f32(k), _f32(v)
-        if pi is not None:
-            idx = np.asarray(pi, dtype=np.int64)[:, :, None]
-            k = np.take_along_axis(k, idx, axis=1)
         self.sq, self.sk, self.dv = q.shape[1], k.shape[1], v.shape[2]
-        qf, kf = preprocess_qk(q, k, k_smooth=k_smooth, qk_hadamard=qk_hadamard)
+        qf, kf = preprocess_qk(q, k, k_smooth=k_smooth, qk_hadamard=qk_hadamard, pi=pi)
         self.w = qf.shape[2]
         self.q8, self.qs = quantize_blocks(qf, q_block)
         self.k8, self.ks = quantize_blocks(kf, k_quant_block)

@@ -11,7 +11,8 @@
  * unspecified (torch .mean / .sum / scatter_add / BLAS), this file fixes one
  * order and the CUDA kernels use exactly the same one:
  *
- *   K channel mean   : per head, rows are split into chunks of VCO_KSUM_CHUNK
+ *   K channel mean   : per head, in original token order (before any
+ *                      permutation), rows are split into chunks of VCO_KSUM_CHUNK
  *                      rows; inside a chunk, row r goes to lane (r % LANES);
  *                      each lane sums its rows in increasing order, the chunk
  *                      sum adds lanes 0..LANES-1 in order, the head total adds

@@ -1,0 +1,259 @@
+// Per-head V clustering for sm_100a: Lloyd k-means with equispaced (or
+// warm-started) centres and a stable permutation of the final labels
+// (reference: core.py:138-163; the Hopper extension drove ATen ops from a
+// host loop, bindings.cpp:182-217).
+//
+// Fixed orders, mirrored by the CPU checker:
+//   distances  ||x||^2, ||c||^2 and x.c are fmaf chains over channels
+//              0..D-1; distance = (xx + cc) - 2*xc; the first minimum wins.
+//   sums       chunks of kChunk tokens; inside a chunk each cluster adds its
+//              tokens in token order; chunks are added in order.
+//   permutation  a counting sort: cluster-major, token order inside a
+//              cluster, i.e. argsort(labels, stable=True).
+#include "vcb_internal.h"
+
+namespace vcb {
+
+constexpr int kChunk = 256;
+constexpr int kMaxClusters = 32;
+
+struct ClusterArgs {
+    const void* v;
+    int64_t S;
+    int D;
+    int count;
+    int nchunk;
+    float* centers;   // [heads, count, D]
+    uint8_t* labels;  // [heads, S]
+    float* psum;      // [heads, nchunk, count, 128]
+    int32_t* pcnt;    // [heads, nchunk, count]
+    int32_t* off;     // [heads, nchunk, count]
+    int32_t* pi;      // [heads, S]
+};
+
+struct InitIdx { long long idx[kMaxClusters]; };
+
+template <typename T>
+__global__ void cluster_init_kernel(ClusterArgs a, const float* __restrict__ centers_in, InitIdx init) {
+    const int64_t h = blockIdx.x;
+    for (int i = threadIdx.x; i < a.count * a.D; i += blockDim.x) {
+        const int c = i / a.D, d = i % a.D;
+        float val;
+        if (centers_in) val = centers_in[(h * a.count + c) * a.D + d];
+        else val = Elem<T>::load(static_cast<const T*>(a.v) + (h * a.S + init.idx[c]) * a.D + d);
+        a.centers[(h * a.count + c) * a.D + d] = val;
+    }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) cluster_assign_kernel(ClusterArgs a) {
+    __shared__ __align__(16) float cen[kMaxClusters * 128];
+    __shared__ float cnorm[kMaxClusters];
+    __shared__ uint8_t lab[kChunk];
+    const int64_t h = blockIdx.y;
+    const int chunk = blockIdx.x;
+    const int tid = threadIdx.x;
+    const int D = a.D, count = a.count;
+    for (int i = tid; i < kMaxClusters * 128; i += 256) {
+        const int c = i / 128, d = i % 128;
+        cen[i] = (c < count && d < D) ? a.centers[(h * count + c) * D + d] : 0.0f;
+    }
+    __syncthreads();
+    if (tid < count) {
+        float acc = 0.0f;
+        for (int d = 0; d < D; ++d) acc = fmaf(cen[tid * 128 + d], cen[tid * 128 + d], acc);
+        cnorm[tid] = acc;
+    }
+    __syncthreads();
+    const int64_t base = (int64_t)chunk * kChunk;
+    const int nvalid = (int)min((int64_t)kChunk, a.S - base);
+    const T* vh = static_cast<const T*>(a.v) + h * a.S * D;
+    if (tid < nvalid) {
+        float x[128];
+        const T* row = vh + (base + tid) * D;
+        if (D == 128) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) load8(row + 8 * i, x + 8 * i);
+        } else {
+#pragma unroll
+            for (int d = 0; d < 128; ++d) x[d] = d < D ? Elem<T>::load(row + d) : 0.0f;
+        }
+        float xx = 0.0f;
+#pragma unroll
+        for (int d = 0; d < 128; ++d)
+            if (d < D) xx = fmaf(x[d], x[d], xx);
+        int best = 0;
+        float bestd = 0.0f;
+        for (int c0 = 0; c0 < count; c0 += 8) {
+            float acc[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+#pragma unroll
+            for (int d = 0; d < 128; d += 4) {
+                if (d < D) {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const float4 cv = *reinterpret_cast<const float4*>(&cen[(c0 + i) * 128 + d]);
+                        acc[i] = fmaf(x[d], cv.x, acc[i]);
+                        if (d + 1 < D) acc[i] = fmaf(x[d + 1], cv.y, acc[i]);
+                        if (d + 2 < D) acc[i] = fmaf(x[d + 2], cv.z, acc[i]);
+                        if (d + 3 < D) acc[i] = fmaf(x[d + 3], cv.w, acc[i]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int c = c0 + i;
+                if (c < count) {
+                    const float dist = __fsub_rn(__fadd_rn(xx, cnorm[c]), __fmul_rn(2.0f, acc[i]));
+                    if (c == 0 || dist < bestd) { bestd = dist; best = c; }
+                }
+            }
+        }
+        lab[tid] = (uint8_t)best;
+        a.labels[h * a.S + base + tid] = (uint8_t)best;
+    }
+    __syncthreads();
+    // Per-cluster partial sums in token order.  Thread (d, parity) owns
+    // clusters parity, parity + 2, ...; adding +0.0 for other tokens leaves
+    // every partial sum bit-identical to adding only the matching tokens.
+    const int d = tid & 127, parity = tid >> 7;
+    float acc[kMaxClusters / 2];
+#pragma unroll
+    for (int i = 0; i < kMaxClusters / 2; ++i) acc[i] = 0.0f;
+    if (d < D) {
+        for (int j = 0; j < nvalid; ++j) {
+            const float val = Elem<T>::load(vh + (base + j) * D + d);
+            const int lj = lab[j];
+#pragma unroll
+            for (int i = 0; i < kMaxClusters / 2; ++i) {
+                const int c = parity + 2 * i;
+                if (c < count) acc[i] += (lj == c) ? val : 0.0f;
+            }
+        }
+    }
+    float* ps = a.psum + ((int64_t)h * a.nchunk + chunk) * count * 128;
+#pragma unroll
+    for (int i = 0; i < kMaxClusters / 2; ++i) {
+        const int c = parity + 2 * i;
+        if (c < count) ps[c * 128 + d] = acc[i];
+    }
+    if (tid < count) {
+        int n = 0;
+        for (int j = 0; j < nvalid; ++j) n += lab[j] == tid;
+        a.pcnt[((int64_t)h * a.nchunk + chunk) * count + tid] = n;
+    }
+}
+
+__global__ void __launch_bounds__(256) cluster_update_kernel(ClusterArgs a) {
+    const int64_t h = blockIdx.x;
+    for (int i = threadIdx.x; i < a.count * 128; i += 256) {
+        const int c = i / 128, d = i % 128;
+        if (d >= a.D) continue;
+        float total = 0.0f;
+        long long n = 0;
+        for (int ch = 0; ch < a.nchunk; ++ch) {
+            total += a.psum[(((int64_t)h * a.nchunk + ch) * a.count + c) * 128 + d];
+            n += a.pcnt[((int64_t)h * a.nchunk + ch) * a.count + c];
+        }
+        if (n > 0) a.centers[(h * a.count + c) * a.D + d] = total / (float)n;
+    }
+}
+
+__global__ void cluster_offsets_kernel(ClusterArgs a) {
+    const int64_t h = blockIdx.x;
+    if (threadIdx.x != 0) return;
+    int running = 0;
+    for (int c = 0; c < a.count; ++c)
+        for (int ch = 0; ch < a.nchunk; ++ch) {
+            const int64_t i = ((int64_t)h * a.nchunk + ch) * a.count + c;
+            a.off[i] = running;
+            running += a.pcnt[i];
+        }
+}
+
+__global__ void __launch_bounds__(256) cluster_scatter_kernel(ClusterArgs a) {
+    __shared__ uint8_t lab[kChunk];
+    const int64_t h = blockIdx.y;
+    const int chunk = blockIdx.x;
+    const int64_t base = (int64_t)chunk * kChunk;
+    const int nvalid = (int)min((int64_t)kChunk, a.S - base);
+    const int j = threadIdx.x;
+    if (j < nvalid) lab[j] = a.labels[h * a.S + base + j];
+    __syncthreads();
+    if (j >= nvalid) return;
+    const int c = lab[j];
+    int rank = 0;
+    for (int i = 0; i < j; ++i) rank += lab[i] == c;
+    const int dst = a.off[((int64_t)h * a.nchunk + chunk) * a.count + c] + rank;
+    a.pi[h * a.S + dst] = (int32_t)(base + j);
+}
+
+namespace {
+
+void linspace_indices(int64_t S, int count, long long* out) {
+    // torch.linspace(0, S-1, count) in float32, then .long() (core.py:148):
+    // first half start + i*step, second half end - (count-1-i)*step.
+    if (count == 1) { out[0] = 0; return; }
+    volatile float start = 0.0f, end = (float)(S - 1);
+    const float step = (end - start) / (float)(count - 1);
+    const int half = count / 2;
+    for (int i = 0; i < count; ++i) {
+        volatile float prod = i < half ? step * (float)i : step * (float)(count - 1 - i);
+        const float val = i < half ? start + prod : end - prod;
+        out[i] = (long long)val;
+    }
+}
+
+template <typename T>
+int run(const vcb_group_args* p, cudaStream_t st) {
+    const int count = (int)(p->clusters < p->s ? p->clusters : p->s);
+    const int nchunk = (int)((p->s + kChunk - 1) / kChunk);
+    char* ws = static_cast<char*>(p->workspace);
+    ClusterArgs a{};
+    a.v = p->v; a.S = p->s; a.D = p->d; a.count = count; a.nchunk = nchunk;
+    a.centers = p->centers_out; a.pi = p->pi;
+    size_t o = 0;
+    auto take = [&](size_t bytes) { char* r = ws + o; o += (bytes + 255) & ~size_t(255); return r; };
+    a.labels = reinterpret_cast<uint8_t*>(take((size_t)p->heads * p->s));
+    a.psum = reinterpret_cast<float*>(take((size_t)p->heads * nchunk * count * 128 * sizeof(float)));
+    a.pcnt = reinterpret_cast<int32_t*>(take((size_t)p->heads * nchunk * count * sizeof(int32_t)));
+    a.off = reinterpret_cast<int32_t*>(take((size_t)p->heads * nchunk * count * sizeof(int32_t)));
+    InitIdx init{};
+    linspace_indices(p->s, count, init.idx);
+    cluster_init_kernel<T><<<(unsigned)p->heads, 256, 0, st>>>(a, p->centers_in, init);
+    VCB_CUDA(cudaGetLastError());
+    for (int it = 0; it < p->iterations; ++it) {
+        cluster_assign_kernel<T><<<dim3(nchunk, (unsigned)p->heads), 256, 0, st>>>(a);
+        VCB_CUDA(cudaGetLastError());
+        cluster_update_kernel<<<(unsigned)p->heads, 256, 0, st>>>(a);
+        VCB_CUDA(cudaGetLastError());
+    }
+    cluster_offsets_kernel<<<(unsigned)p->heads, 32, 0, st>>>(a);
+    VCB_CUDA(cudaGetLastError());
+    cluster_scatter_kernel<<<dim3(nchunk, (unsigned)p->heads), 256, 0, st>>>(a);
+    VCB_CUDA(cudaGetLastError());
+    return VCB_OK;
+}
+
+}  // namespace
+
+size_t group_workspace_bytes(int64_t heads, int64_t s, int d, int clusters) {
+    (void)d;
+    const int64_t count = clusters < s ? clusters : s;
+    const int64_t nchunk = (s + kChunk - 1) / kChunk;
+    auto r = [](size_t b) { return (b + 255) & ~size_t(255); };
+    return r((size_t)(heads * s)) + r((size_t)(heads * nchunk * count * 128 * 4)) +
+           2 * r((size_t)(heads * nchunk * count * 4));
+}
+
+int group_run(const vcb_group_args* p, cudaStream_t st) {
+    switch (p->dtype) {
+        case VCB_F32: return run<float>(p, st);
+        case VCB_F16: return run<__half>(p, st);
+        case VCB_BF16: return run<__nv_bfloat16>(p, st);
+        default: return fail(VCB_ERR_INVALID_ARGUMENT, "unknown dtype %d", p->dtype);
+    }
+}
+
+}  // namespace vcb

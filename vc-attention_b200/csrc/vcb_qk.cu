@@ -1,0 +1,378 @@
+// Q/K preprocessing for sm_100a: post-RoPE K channel demean, normalised
+// Sylvester Hadamard and per-block E4M3 quantisation, fused into one pass per
+// quantisation block (reference: core.py:71-99 and :118-135; the Hopper
+// extension ran these as kernels.cu:72-120 plus an ATen mean).
+//
+// Reduction orders are fixed and mirrored by the CPU checker:
+//   K mean: chunks of kKsumChunk rows; inside a chunk row r goes to lane
+//   r % kKsumLanes, lanes sum their rows in increasing order, the chunk sum
+//   adds lanes in order, the head total adds chunks in order, then / S.
+#include "vcb_internal.h"
+
+namespace vcb {
+
+constexpr int kKsumChunk = 256;
+constexpr int kKsumLanes = 16;
+
+template <typename T>
+__global__ void __launch_bounds__(256) k_colsum_kernel(const T* __restrict__ k, int64_t S, int D,
+                                                       float* __restrict__ partial, int nchunk) {
+    __shared__ float part[kKsumLanes][128];
+    const int64_t h = blockIdx.y;
+    const int chunk = blockIdx.x;
+    const int t = threadIdx.x, lane = t / 16, g = t % 16;
+    const int64_t base = (int64_t)chunk * kKsumChunk;
+    const int64_t end = min(base + (int64_t)kKsumChunk, S);
+    const T* kh = k + h * S * D;
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+    if (D == 128) {
+        for (int64_t r = base + lane; r < end; r += kKsumLanes) {
+            float x[8];
+            load8(kh + r * 128 + 8 * g, x);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] += x[i];
+        }
+    } else {
+        for (int64_t r = base + lane; r < end; r += kKsumLanes) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int c = 8 * g + i;
+                if (c < D) acc[i] += Elem<T>::load(kh + r * D + c);
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) part[lane][8 * g + i] = acc[i];
+    __syncthreads();
+    if (t < 128) {
+        float s = 0.0f;
+#pragma unroll
+        for (int l = 0; l < kKsumLanes; ++l) s += part[l][t];
+        partial[((int64_t)h * nchunk + chunk) * 128 + t] = s;
+    }
+}
+
+__global__ void k_mean_kernel(const float* __restrict__ partial, int nchunk, int64_t S,
+                              float* __restrict__ mean) {
+    const int64_t h = blockIdx.x;
+    const int c = threadIdx.x;
+    float total = 0.0f;
+    for (int ch = 0; ch < nchunk; ++ch) total += partial[((int64_t)h * nchunk + ch) * 128 + c];
+    mean[h * 128 + c] = total / (float)S;
+}
+
+struct RowArgs {
+    const void* x;
+    int64_t S;
+    int D;
+    int width;          // output width: next pow2 >= D with the Hadamard, else D
+    int hadamard;
+    float norm;         // fp32(width^-0.5)
+    const int32_t* pi;  // row permutation or null
+    const float* mean;  // [heads, 128] or null
+    int block;          // quantisation block rows
+    int64_t S_pad;
+    int nblk;           // ceil(S / block)
+    uint8_t* payload;   // [heads, S_pad, 128]
+    float* scales;      // [heads, nblk]
+    float* out_f32;     // [heads, S, width] (transform-only mode)
+    int32_t* status;
+};
+
+// Loads row `r` (through the permutation) and applies demean + Hadamard.
+template <typename T>
+__device__ __forceinline__ bool transform_row(const RowArgs& a, int64_t h, int64_t r, const float* smean,
+                                              float (&x)[128]) {
+    const int64_t tok = a.pi ? (int64_t)a.pi[h * a.S + r] : r;
+    const T* src = static_cast<const T*>(a.x) + (h * a.S + tok) * a.D;
+    bool ok = true;
+    if (a.D == 128) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) load8(src + 8 * i, x + 8 * i);
+    } else {
+#pragma unroll
+        for (int c = 0; c < 128; ++c) x[c] = c < a.D ? Elem<T>::load(src + c) : 0.0f;
+    }
+#pragma unroll
+    for (int c = 0; c < 128; ++c) ok &= finite_f(x[c]);
+    if (smean) {
+#pragma unroll
+        for (int c = 0; c < 128; ++c)
+            if (c < a.D) x[c] = x[c] - smean[c];
+    }
+    if (a.hadamard) {
+        // Butterflies with stride 1, 2, 4, ... (core.py:79-84): (l + r, l - r).
+        // Running a stage over the zero-padded 128 array leaves [0, width)
+        // exactly the width-point transform and the padding at zero.
+#pragma unroll
+        for (int s = 1; s < 128; s <<= 1) {
+            if (s < a.width) {
+#pragma unroll
+                for (int base = 0; base < 128; base += 2 * s) {
+#pragma unroll
+                    for (int t = 0; t < s; ++t) {
+                        const float l = x[base + t], rr = x[base + s + t];
+                        x[base + t] = l + rr;
+                        x[base + s + t] = l - rr;
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int c = 0; c < 128; ++c)
+            if (c < a.width) x[c] = x[c] * a.norm;
+    }
+    return ok;
+}
+
+// Half-row form used by the quantiser: a lane pair (lane, lane ^ 16) holds
+// one row, the lower lane channels [0, 64), the upper lane [64, 128).  The
+// butterflies with stride 1..32 stay inside a half; the stride-64 stage
+// exchanges halves with one shuffle per element and still computes
+// (left + right, left - right) on the same operands.
+template <typename T>
+__device__ __forceinline__ bool transform_half(const RowArgs& a, int64_t h, int64_t r, bool valid, int half,
+                                               const float* smean, float (&x)[64]) {
+    bool ok = true;
+    const int c0 = 64 * half;
+    if (valid) {
+        const int64_t tok = a.pi ? (int64_t)a.pi[h * a.S + r] : r;
+        const T* src = static_cast<const T*>(a.x) + (h * a.S + tok) * a.D;
+        if (a.D == 128) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) load8(src + c0 + 8 * i, x + 8 * i);
+        } else {
+#pragma unroll
+            for (int c = 0; c < 64; ++c) x[c] = c0 + c < a.D ? Elem<T>::load(src + c0 + c) : 0.0f;
+        }
+#pragma unroll
+        for (int c = 0; c < 64; ++c) ok &= finite_f(x[c]);
+        if (smean) {
+#pragma unroll
+            for (int c = 0; c < 64; ++c)
+                if (c0 + c < a.D) x[c] = x[c] - smean[c0 + c];
+        }
+    } else {
+#pragma unroll
+        for (int c = 0; c < 64; ++c) x[c] = 0.0f;
+    }
+    if (a.hadamard) {
+#pragma unroll
+        for (int s = 1; s < 64; s <<= 1) {
+            if (s < a.width) {
+#pragma unroll
+                for (int base = 0; base < 64; base += 2 * s) {
+#pragma unroll
+                    for (int t = 0; t < s; ++t) {
+                        const float l = x[base + t], rr = x[base + s + t];
+                        x[base + t] = l + rr;
+                        x[base + s + t] = l - rr;
+                    }
+                }
+            }
+        }
+        if (a.width > 64) {
+#pragma unroll
+            for (int c = 0; c < 64; ++c) {
+                const float other = __shfl_xor_sync(0xffffffffu, x[c], 16);
+                x[c] = half == 0 ? x[c] + other : other - x[c];
+            }
+        }
+#pragma unroll
+        for (int c = 0; c < 64; ++c)
+            if (c0 + c < a.width) x[c] = x[c] * a.norm;
+    }
+    return ok;
+}
+
+// 64 E4M3 bytes of a half row: x / scale as div_by(x * pre, bdiv, rdiv)
+// (the correctly rounded quotient), clamped to +-448.
+__device__ __forceinline__ void encode_half(const float (&x)[64], int c0, int W, float pre, float bdiv,
+                                            float rdiv, uint4* dst) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        uint32_t w[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            float v[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int c = 16 * q + 4 * k + e;
+                v[e] = c0 + c < W ? clamp448(div_by(__fmul_rn(x[c], pre), bdiv, rdiv)) : 0.0f;
+            }
+            w[k] = e4m3x2(v[0], v[1]) | (e4m3x2(v[2], v[3]) << 16);
+        }
+        dst[q] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
+// One CTA per quantisation block, two threads per row, 256 rows per pass.
+// Blocks of at most 256 rows keep the transformed halves in registers from
+// the amax to the encode; larger blocks re-read and re-transform in pass 2.
+template <typename T>
+__global__ void __launch_bounds__(512) qk_quant_kernel(RowArgs a) {
+    __shared__ float smean[128];
+    __shared__ float red[16];
+    __shared__ float sdiv[3];
+    const int64_t h = blockIdx.y;
+    const int b = blockIdx.x;
+    const int nthr = blockDim.x;
+    if (a.mean)
+        for (int c = threadIdx.x; c < 128; c += nthr) smean[c] = a.mean[h * 128 + c];
+    __syncthreads();
+    const float* sm = a.mean ? smean : nullptr;
+    const int W = a.hadamard ? a.width : a.D;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int half = lane >> 4;
+    const int rows_per_pass = nthr / 2;
+    const int64_t r0 = (int64_t)b * a.block;
+    const bool single = a.block <= rows_per_pass;
+    float x[64];
+    float amax = 0.0f;
+    bool ok = true;
+    for (int base = 0; base < a.block; base += rows_per_pass) {
+        const int rl = base + warp * 16 + (lane & 15);
+        const int64_t r = r0 + rl;
+        const bool valid = rl < a.block && r < a.S;
+        ok &= transform_half<T>(a, h, r, valid, half, sm, x);
+#pragma unroll
+        for (int c = 0; c < 64; ++c)
+            if (64 * half + c < W) amax = fmaxf(amax, fabsf(x[c]));
+    }
+    if (!ok) flag_status(a.status, VCB_FLAG_NONFINITE);
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if (lane == 0) red[warp] = amax;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float bmax = 0.0f;
+        for (int w = 0; w < nthr / 32; ++w) bmax = fmaxf(bmax, red[w]);
+        float scale = bmax / 448.0f;
+        if (scale == 0.0f) scale = 1.0f;
+        if (b < a.nblk) a.scales[h * a.nblk + b] = scale;
+        const float pre = div_prescale(scale);
+        sdiv[0] = pre;
+        sdiv[1] = scale * pre;
+        sdiv[2] = __frcp_rn(scale * pre);
+    }
+    __syncthreads();
+    const float pre = sdiv[0], bdiv = sdiv[1], rdiv = sdiv[2];
+    for (int base = 0; base < a.block; base += rows_per_pass) {
+        const int rl = base + warp * 16 + (lane & 15);
+        const int64_t r = r0 + rl;
+        const bool valid = rl < a.block && r < a.S;
+        if (!single) transform_half<T>(a, h, r, valid, half, sm, x);   // warp-uniform
+        if (rl >= a.block || r >= a.S_pad) continue;
+        uint4* dst = reinterpret_cast<uint4*>(a.payload + (h * a.S_pad + r) * 128 + 64 * half);
+        if (!valid) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) dst[q] = make_uint4(0u, 0u, 0u, 0u);
+            continue;
+        }
+        encode_half(x, 64 * half, W, pre, bdiv, rdiv, dst);
+    }
+}
+
+// Transform-only rows (the preprocess_qk export): one row per thread.
+template <typename T>
+__global__ void __launch_bounds__(128) qk_transform_kernel(RowArgs a) {
+    __shared__ float smean[128];
+    const int64_t h = blockIdx.y;
+    if (a.mean) smean[threadIdx.x] = a.mean[h * 128 + threadIdx.x];
+    __syncthreads();
+    const int64_t r = (int64_t)blockIdx.x * 128 + threadIdx.x;
+    if (r >= a.S) return;
+    float x[128];
+    transform_row<T>(a, h, r, a.mean ? smean : nullptr, x);
+    const int W = a.hadamard ? a.width : a.D;
+    float* dst = a.out_f32 + (h * a.S + r) * W;
+#pragma unroll
+    for (int c = 0; c < 128; ++c)
+        if (c < W) dst[c] = x[c];
+}
+
+namespace {
+
+int width_for(int d, int hadamard) {
+    if (!hadamard) return d;
+    int w = 1;
+    while (w < d) w <<= 1;
+    return w;
+}
+
+template <typename T>
+int launch_k_mean(const void* k, int64_t heads, int64_t S, int D, float* partial, float* mean,
+                  cudaStream_t st) {
+    const int nchunk = (int)((S + kKsumChunk - 1) / kKsumChunk);
+    k_colsum_kernel<T><<<dim3(nchunk, (unsigned)heads), 256, 0, st>>>(static_cast<const T*>(k), S, D,
+                                                                       partial, nchunk);
+    VCB_CUDA(cudaGetLastError());
+    k_mean_kernel<<<(unsigned)heads, 128, 0, st>>>(partial, nchunk, S, mean);
+    VCB_CUDA(cudaGetLastError());
+    return VCB_OK;
+}
+
+template <typename T>
+int launch_rows(const RowArgs& a, int64_t heads, bool quantise, cudaStream_t st) {
+    if (quantise) {
+        const unsigned grid = (unsigned)(a.S_pad / a.block);
+        const int rows = a.block < 256 ? a.block : 256;
+        const int nthr = (rows + 15) / 16 * 32;      // two threads per row, whole warps
+        qk_quant_kernel<T><<<dim3(grid, (unsigned)heads), nthr, 0, st>>>(a);
+    } else {
+        qk_transform_kernel<T><<<dim3((unsigned)((a.S + 127) / 128), (unsigned)heads), 128, 0, st>>>(a);
+    }
+    VCB_CUDA(cudaGetLastError());
+    return VCB_OK;
+}
+
+template <typename T>
+int run_qk(const vcb_qk_args* p, bool quantise, cudaStream_t st) {
+    const int width = width_for(p->d, p->hadamard);
+    const float norm = (float)pow((double)width, -0.5);
+    float* mean = nullptr;
+    if (p->k_smooth) {
+        float* ws = static_cast<float*>(p->workspace);
+        mean = ws;                                   // [heads, 128]
+        float* partial = ws + p->heads * 128;        // [heads, nchunk, 128]
+        int rc = launch_k_mean<T>(p->k, p->heads, p->sk, p->d, partial, mean, st);
+        if (rc) return rc;
+    }
+    RowArgs q{};
+    q.x = p->q; q.S = p->sq; q.D = p->d; q.width = width; q.hadamard = p->hadamard; q.norm = norm;
+    q.pi = nullptr; q.mean = nullptr; q.status = p->status;
+    RowArgs k = q;
+    k.x = p->k; k.S = p->sk; k.pi = p->pi; k.mean = mean;
+    if (quantise) {
+        q.block = p->q_block; q.S_pad = vcb_padded_rows(p->sq, p->q_block);
+        q.nblk = (int)((p->sq + p->q_block - 1) / p->q_block); q.payload = p->q8; q.scales = p->q_scale;
+        k.block = p->k_quant_block; k.S_pad = vcb_padded_rows(p->sk, p->k_quant_block);
+        k.nblk = (int)((p->sk + p->k_quant_block - 1) / p->k_quant_block); k.payload = p->k8;
+        k.scales = p->k_scale;
+    } else {
+        q.out_f32 = p->q_out;
+        k.out_f32 = p->k_out;
+    }
+    int rc = launch_rows<T>(q, p->heads, quantise, st);
+    if (rc) return rc;
+    return launch_rows<T>(k, p->heads, quantise, st);
+}
+
+}  // namespace
+
+size_t qk_workspace_bytes(int64_t heads, int64_t sk) {
+    const int64_t nchunk = (sk + kKsumChunk - 1) / kKsumChunk;
+    return (size_t)(heads * 128 + heads * nchunk * 128) * sizeof(float);
+}
+
+int qk_run(const vcb_qk_args* p, bool quantise, cudaStream_t st) {
+    switch (p->dtype) {
+        case VCB_F32: return run_qk<float>(p, quantise, st);
+        case VCB_F16: return run_qk<__half>(p, quantise, st);
+        case VCB_BF16: return run_qk<__nv_bfloat16>(p, quantise, st);
+        default: return fail(VCB_ERR_INVALID_ARGUMENT, "unknown dtype %d", p->dtype);
+    }
+}
+
+}  // namespace vcb

@@ -1,0 +1,117 @@
+// V tile preparation for sm_100a (reference: core.py:102-115 per kv_block
+// tile at core.py:300-304, after the permutation of core.py:288-290; the
+// Hopper extension used one CTA per (tile, channel), kernels.cu:124-162, and
+// gathered V in PyTorch, cuda_backend.py:51).
+//
+// One CTA per (head, 128-token tile): the tile's tokens are gathered through
+// the permutation with coalesced row loads into shared memory (fp32), then
+// thread c owns channel c: block mean (tokens added in tile order), residual,
+// per-channel scale with the mean-dtype finite-storage guard, E4M3 residual
+// written channel-major (the K-major B operand of the PV MMA), and the
+// scaled mean rounded to the mean dtype.
+#include "vcb_internal.h"
+
+namespace vcb {
+
+constexpr int kTile = 128;
+
+template <typename T>
+__global__ void __launch_bounds__(128) vprep_kernel(const T* __restrict__ v, int64_t S, int dv,
+                                                    const int32_t* __restrict__ pi, int active,
+                                                    int mean_type, int T_tiles, uint8_t* __restrict__ v8,
+                                                    float* __restrict__ meta, int32_t* status) {
+    extern __shared__ float tile[];          // [kTile][128]
+    const int64_t h = blockIdx.y;
+    const int t = blockIdx.x;
+    const int64_t s0 = (int64_t)t * kTile;
+    const int cnt = (int)min((int64_t)kTile, S - s0);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    bool ok = true;
+    for (int j = warp; j < kTile; j += 4) {
+        float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (j < cnt) {
+            const int64_t tok = pi ? (int64_t)pi[h * S + s0 + j] : s0 + j;
+            const T* row = v + (h * S + tok) * dv;
+            float e[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int c = 4 * lane + i;
+                e[i] = c < dv ? Elem<T>::load(row + c) : 0.0f;
+                ok &= finite_f(e[i]);
+            }
+            f = make_float4(e[0], e[1], e[2], e[3]);
+        }
+        reinterpret_cast<float4*>(tile + j * 128)[lane] = f;
+    }
+    if (!ok) flag_status(status, VCB_FLAG_NONFINITE);
+    __syncthreads();
+    const int c = threadIdx.x;
+    const int64_t m = ((int64_t)h * T_tiles + t);
+    uint32_t packed[32];
+    float scale = 1.0f, stored = 0.0f;
+    if (c < dv) {
+        float mean = 0.0f;
+        if (active) {
+            float sum = 0.0f;
+            for (int j = 0; j < cnt; ++j) sum += tile[j * 128 + c];
+            mean = sum / (float)cnt;
+        }
+        float amax = 0.0f;
+        for (int j = 0; j < cnt; ++j) amax = fmaxf(amax, fabsf(tile[j * 128 + c] - mean));
+        scale = amax / 448.0f;
+        if (scale == 0.0f) scale = 1.0f;
+        const float limit = mean_type == 1 ? 65504.0f : mean_type == 2 ? 3.3895313892515355e38f : 3.4028234663852886e38f;
+        scale = fmaxf(scale, fabsf(mean) / limit);
+        const float pre = div_prescale(scale);
+        const float bdiv = scale * pre;
+        const float rdiv = __frcp_rn(bdiv);
+#pragma unroll
+        for (int w = 0; w < 32; ++w) {
+            float q[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int j = 4 * w + e;
+                const float r = tile[j * 128 + c] - mean;
+                q[e] = j < cnt ? clamp448(div_by(__fmul_rn(r, pre), bdiv, rdiv)) : 0.0f;
+            }
+            packed[w] = e4m3x2(q[0], q[1]) | (e4m3x2(q[2], q[3]) << 16);
+        }
+        const float sm = __fdiv_rn(mean, scale);
+        stored = mean_type == 1 ? __half2float(__float2half_rn(sm))
+               : mean_type == 2 ? __bfloat162float(__float2bfloat16_rn(sm)) : sm;
+    } else {
+#pragma unroll
+        for (int w = 0; w < 32; ++w) packed[w] = 0u;
+    }
+    uint4* dst = reinterpret_cast<uint4*>(v8 + (m * 128 + c) * kTile);
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+        dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+    meta[m * 256 + c] = scale;
+    meta[m * 256 + 128 + c] = stored;
+}
+
+namespace {
+template <typename T>
+int launch(const vcb_v_args* p, cudaStream_t st) {
+    const int T_tiles = (int)((p->s + kTile - 1) / kTile);
+    const size_t smem = kTile * 128 * sizeof(float);
+    VCB_CUDA(cudaFuncSetAttribute(vprep_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    vprep_kernel<T><<<dim3(T_tiles, (unsigned)p->heads), 128, smem, st>>>(
+        static_cast<const T*>(p->v), p->s, p->dv, p->pi, p->active, p->mean_type, T_tiles, p->v8,
+        p->v_meta, p->status);
+    VCB_CUDA(cudaGetLastError());
+    return VCB_OK;
+}
+}  // namespace
+
+int vprep_run(const vcb_v_args* p, cudaStream_t st) {
+    switch (p->dtype) {
+        case VCB_F32: return launch<float>(p, st);
+        case VCB_F16: return launch<__half>(p, st);
+        case VCB_BF16: return launch<__nv_bfloat16>(p, st);
+        default: return fail(VCB_ERR_INVALID_ARGUMENT, "unknown dtype %d", p->dtype);
+    }
+}
+
+}  // namespace vcb

@@ -94,13 +94,16 @@ class LayoutCache:
 
     def _snapshot(self, layer_id):
         state = self._states.get(layer_id)
-        return (self._request_id, dict(self._states), None if state is None else dict(state))
+        return (self._request_id, dict(self._states), state, None if state is None else dict(state))
 
     def _restore(self, snap, layer_id):
-        request_id, states, state = snap
+        """Undo a layout() call whose forward failed (the same state objects come back)."""
+        request_id, states, state, fields = snap
         self._request_id = request_id
         self._states = states
         if state is not None:
+            state.clear()
+            state.update(fields)
             self._states[layer_id] = state
 
     def layout(self, v, *, step, total_steps, request_id, layer_id):

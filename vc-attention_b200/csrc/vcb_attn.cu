@@ -3,33 +3,36 @@
 // Replaces the reference's host loop over heads x Q tiles x KV tiles
 // (kernels.cu:313-330: a cuBLASLt E4M3 GEMM for S, softmax_update, a second
 // GEMM for PV and accumulate, all through HBM scratch) with one CTA per
-// (head, 128-row Q tile) that keeps every intermediate on chip:
+// (head, 128-row Q tile) that keeps every intermediate on chip.
 //
-//   warp 0      TMA producer: Q tile once, then K / V / V-metadata tiles into
-//               a 4-stage ring (no cluster multicast).
+// Roles (512 threads, register budgets rebalanced with setmaxnreg):
+//   warp 0      TMA producer: the Q tile once, then K / V / V-metadata tiles
+//               into a 4-stage ring (no cluster multicast).
 //   warp 1      MMA issuer (one thread): S_j = Q8 K8_j^T into TMEM
-//               (tcgen05.mma kind::f8f6f4, E4M3 x E4M3 -> F32), then
-//               O_j = P_j R_j with P read from TMEM.  In ExpCast mode V carries
-//               16 extra rows of E4M3 ones, so column 128 of O_j is the row
-//               mass sum(decode(P_j)) produced by the tensor core itself.
-//   warps 4-7   softmax: one thread per query row.  Row max, alpha, and either
-//               the ExpCast byte encode (one FMA per score, the f16-subnormal
-//               conversion rounds to the integer code and clamps at zero) or
-//               exp + E4M3(p * 256); P is written back over S in TMEM.
-//   warps 8-15  correction: acc = alpha * acc + (O_j + M_j * mu_j) * vscale_j
-//               per row and channel (two threads per row, 64 channels each),
-//               den = alpha * den + M_j; epilogue acc / den in the output dtype.
+//               (tcgen05.mma kind::f8f6f4, E4M3 x E4M3 -> F32) and
+//               O_j = P_j R_j with P_j and R_j in shared memory.
+//   warps 4-7   softmax, one thread per query row: one TMEM read of the
+//               128 scores, row max, alpha, the ExpCast byte encode (one
+//               packed FMA per pair of scores; the f16-subnormal conversion
+//               rounds to the integer code and clamps it at zero) or
+//               exp + E4M3(p * 256); the row mass; P_j into shared memory.
+//   warps 8-15  correction, two threads per row (64 channels each):
+//               acc = alpha acc + (O_j + M_j mu_j) vscale_j,
+//               den = alpha den + M_j; epilogue acc / den in the output dtype.
+//
+// Latency hiding: S and O are double-buffered in TMEM (S0, S1, O0, O1 use all
+// 512 columns).  The softmax releases S_j as soon as it has read it, so
+// QK_{j+2} runs while the softmax of tile j computes; PV_j only waits for
+// the correction of tile j-2.
 //
 // Numerical contract (core.py:307-341): S = (q8 . k8) * qs * ks * scale;
 // ExpCast code = rne(clamp(fma(S - m, 8 log2 e, 119.65), 0, 120)) viewed as
-// E4M3 with a 1/256 scale and a decoded row mass; non-ExpCast P8 =
-// e4m3(exp(S - m) * 256) with an FP32 row mass; V-mean recovery lives inside
-// the accumulator and is rescaled with the running max.  Accumulators are
-// kept in units of 256 (acc256 = 256 acc, den256 = 256 den), which changes no
-// rounding because 256 is a power of two.
-//
-// TMEM columns: S0 [0,128), S1 [128,256), O [256, 256+N) with N = 144
-// (ExpCast) or 128.  All mbarrier waits are bounded (vcb_common.cuh).
+// E4M3 with a 1/256 scale, row mass = sum of decoded P; non-ExpCast P8 =
+// e4m3(exp(S - m) * 256) with an FP32 row mass of exp; V-mean recovery lives
+// inside the accumulator and is rescaled with the running max.  The
+// accumulators are kept in units of 256 (acc256 = 256 acc, den256 = 256
+// den); 256 is a power of two, so no rounding changes.  Every mbarrier wait
+// is bounded (vcb_common.cuh).
 #include "vcb_internal.h"
 
 namespace vcb {
@@ -40,20 +43,21 @@ constexpr int kBM = 128;
 constexpr int kBN = 128;
 constexpr int kStages = 4;
 constexpr int kThreads = 512;
-constexpr uint32_t kTile = 128 * 128;            // one E4M3 tile
-constexpr uint32_t kVBytes = kTile + 16 * 128;   // + 16 rows of ones
+constexpr uint32_t kTile = 128 * 128;            // one E4M3 tile (16 KB)
 constexpr uint32_t kMetaBytes = 1024;            // vscale[128], mu[128]
-constexpr uint32_t kStageBytes = kTile + kVBytes + kMetaBytes;
+constexpr uint32_t kStageBytes = 2 * kTile + kMetaBytes;
 constexpr uint32_t kOffQ = 0;
-constexpr uint32_t kOffStages = kTile;
+constexpr uint32_t kOffP = kTile;                // P0, P1
+constexpr uint32_t kOffStages = kOffP + 2 * kTile;
 constexpr uint32_t kOffStats = kOffStages + kStages * kStageBytes;   // alpha[4][128], mass[4][128]
 constexpr uint32_t kOffBars = kOffStats + 2 * 4 * 128 * 4;
-constexpr int kNumBars = 1 + 2 * kStages + 2 + 2 + 1 + 1 + 4 + 4 + 1;
+constexpr int kNumBars = 1 + 2 * kStages + 2 * 5 + 2 * 4 + 1;
 constexpr uint32_t kOffMisc = kOffBars + kNumBars * 8;
 constexpr uint32_t kSmemBytes = kOffMisc + 16;
 constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColO = 256;
+constexpr uint32_t kColS = 0;                    // S0, S1
+constexpr uint32_t kColO = 256;                  // O0, O1
 
 constexpr float kC1 = 11.541560173034668f;       // 8 log2(e) in fp32
 constexpr float kC2 = 119.6500015258789f;        // 119.65 in fp32
@@ -69,7 +73,7 @@ struct Params {
     int32_t* status;
     int64_t sq, sk;
     int dv, q_block, kq, nqb, nkb, T;
-    int expcast, has_mean, out_dtype;
+    int out_dtype;
     float scale;
 };
 
@@ -77,11 +81,12 @@ struct Bars {
     uint64_t* q_full;
     uint64_t* kv_full;     // [kStages]
     uint64_t* kv_empty;    // [kStages]
-    uint64_t* s_full;      // [2]
-    uint64_t* p_full;      // [2]
-    uint64_t* o_full;
-    uint64_t* o_free;
-    uint64_t* st_full;     // [4]
+    uint64_t* s_full;      // [2]  QK_j done
+    uint64_t* s_free;      // [2]  softmax has read S_j
+    uint64_t* p_full;      // [2]  P_j in shared memory
+    uint64_t* o_full;      // [2]  PV_j done (also: P buffer free again)
+    uint64_t* o_free;      // [2]  correction has read O_j
+    uint64_t* st_full;     // [4]  alpha / mass of tile j
     uint64_t* st_free;     // [4]
     uint64_t* drain;
 };
@@ -93,9 +98,10 @@ __device__ __forceinline__ Bars bars_at(uint8_t* smem) {
     r.kv_full = b; b += kStages;
     r.kv_empty = b; b += kStages;
     r.s_full = b; b += 2;
+    r.s_free = b; b += 2;
     r.p_full = b; b += 2;
-    r.o_full = b; b += 1;
-    r.o_free = b; b += 1;
+    r.o_full = b; b += 2;
+    r.o_free = b; b += 2;
     r.st_full = b; b += 4;
     r.st_free = b; b += 4;
     r.drain = b;
@@ -133,7 +139,7 @@ __device__ void producer(const Params& p, uint8_t* smem, const Bars& B, volatile
         mbar_arrive_expect_tx(&B.kv_full[s], 2 * kTile + kMetaBytes);
         tma_load_3d(st, &p.tm_k, &B.kv_full[s], 0, j * kBN, head);
         tma_load_3d(st + kTile, &p.tm_v, &B.kv_full[s], 0, j * 128, head);
-        bulk_load(st + kTile + kVBytes, meta + (int64_t)j * 256, kMetaBytes, &B.kv_full[s]);
+        bulk_load(st + 2 * kTile, meta + (int64_t)j * 256, kMetaBytes, &B.kv_full[s]);
         armed[s] = u + 1;
     }
     if (*abort) {   // no TMA write may land after the CTA exits
@@ -144,82 +150,96 @@ __device__ void producer(const Params& p, uint8_t* smem, const Bars& B, volatile
 }
 
 __device__ void mma_issuer(const Params& p, uint8_t* smem, const Bars& B, volatile int* abort, uint32_t tmem) {
-    const uint32_t idesc_qk = idesc_e4m3_f32(kBM, kBN);
-    const uint32_t idesc_pv = idesc_e4m3_f32(kBM, p.expcast ? 144 : 128);
+    const uint32_t idesc = idesc_e4m3_f32(kBM, kBN);
     const uint64_t qdesc = smem_desc_k128(smem + kOffQ);
-    if (mbar_wait(B.q_full, 0, abort)) {
-        for (int j = 0; j <= p.T; ++j) {
-            if (j < p.T) {
-                const int s = j % kStages;
-                if (!mbar_wait(&B.kv_full[s], (j / kStages) & 1, abort)) break;
-                tc_fence_after();
-                const int b = j & 1;
-                const uint64_t kdesc = smem_desc_k128(smem + kOffStages + s * kStageBytes);
+    auto issue_qk = [&](int j) -> bool {
+        const int s = j % kStages;
+        if (!mbar_wait(&B.kv_full[s], (j / kStages) & 1, abort)) return false;
+        tc_fence_after();
+        const uint64_t kdesc = smem_desc_k128(smem + kOffStages + s * kStageBytes);
+        const uint32_t d = tmem + kColS + (j & 1) * kBN;
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    mma_f8_ss(tmem + b * kBN, qdesc + 2 * kk, kdesc + 2 * kk, idesc_qk, kk > 0);
-                mma_commit(&B.s_full[b]);
-            }
-            if (j >= 1) {
-                const int jp = j - 1, bp = jp & 1, sp = jp % kStages;
-                if (!mbar_wait(&B.p_full[bp], (jp >> 1) & 1, abort)) break;
-                if (jp >= 1 && !mbar_wait(B.o_free, (jp - 1) & 1, abort)) break;
-                tc_fence_after();
-                const uint64_t vdesc = smem_desc_k128(smem + kOffStages + sp * kStageBytes + kTile);
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    mma_f8_ts(tmem + kColO, tmem + bp * kBN + kk * 8, vdesc + 2 * kk, idesc_pv, kk > 0);
-                mma_commit(B.o_full);
-                mma_commit(&B.kv_empty[sp]);
-            }
+        for (int kk = 0; kk < 4; ++kk) mma_f8_ss(d, qdesc + 2 * kk, kdesc + 2 * kk, idesc, kk > 0);
+        mma_commit(&B.s_full[j & 1]);
+        return true;
+    };
+    bool ok = mbar_wait(B.q_full, 0, abort);
+    if (ok && p.T > 0) ok = issue_qk(0);
+    if (ok && p.T > 1) ok = issue_qk(1);
+    for (int j = 0; ok && j < p.T; ++j) {
+        const int b = j & 1;
+        if (j + 2 < p.T) {
+            if (!mbar_wait(&B.s_free[b], (j >> 1) & 1, abort) || !issue_qk(j + 2)) break;
         }
+        if (!mbar_wait(&B.p_full[b], (j >> 1) & 1, abort)) break;
+        if (j >= 2 && !mbar_wait(&B.o_free[b], ((j - 2) >> 1) & 1, abort)) break;
+        tc_fence_after();
+        const int s = j % kStages;
+        const uint64_t pdesc = smem_desc_k128(smem + kOffP + b * kTile);
+        const uint64_t vdesc = smem_desc_k128(smem + kOffStages + s * kStageBytes + kTile);
+        const uint32_t d = tmem + kColO + b * 128;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) mma_f8_ss(d, pdesc + 2 * kk, vdesc + 2 * kk, idesc, kk > 0);
+        mma_commit(&B.o_full[b]);
+        mma_commit(&B.kv_empty[s]);
     }
     mma_commit(B.drain);
     drain_wait(B.drain, 0);
 }
 
+template <bool EXPCAST>
 __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, volatile int* abort, uint32_t tmem,
                              int qtile, int head, int quarter, int lane) {
     const int row = quarter * 32 + lane;
     const int64_t grow = (int64_t)qtile * kBM + row;
     int qb = (int)(grow / p.q_block);
     if (qb >= p.nqb) qb = p.nqb - 1;
-    const float qs = p.q_scale[(int64_t)head * p.nqb + qb];
+    const float qs_scale = __fmul_rn(p.q_scale[(int64_t)head * p.nqb + qb], 1.0f);
     const float* ksp = p.k_scale + (int64_t)head * p.nkb;
     float* st_alpha = reinterpret_cast<float*>(smem + kOffStats);
     float* st_mass = st_alpha + 4 * 128;
     const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
+    uint8_t* prow_base = smem + kOffP + row * 128;
+    const uint32_t swz = (uint32_t)(row & 7);
     float m = -INFINITY;
     for (int j = 0; j < p.T; ++j) {
         const int b = j & 1;
+        const float ks = __ldg(ksp + ((int64_t)j * kBN) / p.kq);
         if (!mbar_wait(&B.s_full[b], (j >> 1) & 1, abort)) break;
         tc_fence_after();
+        uint32_t r[128];
+        const uint32_t ts = trow + kColS + b * kBN;
+        tmem_ld32_at<0>(ts, r);
+        tmem_ld32_at<32>(ts + 32, r);
+        tmem_ld32_at<64>(ts + 64, r);
+        tmem_ld32_at<96>(ts + 96, r);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&B.s_free[b]);
         const int nvalid = (int)min((int64_t)kBN, p.sk - (int64_t)j * kBN);
-        const bool tail = nvalid < kBN;
-        const uint32_t ts = trow + b * kBN;
-        float mx = -INFINITY;
+        if (nvalid < kBN) {
 #pragma unroll
-        for (int ch = 0; ch < 4; ++ch) {
-            uint32_t r[32];
-            tmem_ld32(ts + 32 * ch, r);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                float v = __uint_as_float(r[i]);
-                if (tail && 32 * ch + i >= nvalid) v = -INFINITY;
-                mx = fmaxf(mx, v);
-            }
+            for (int i = 0; i < 128; ++i)
+                if (i >= nvalid) r[i] = 0xff800000u;   // -inf: masked key
         }
-        const float ks = ksp[((int64_t)j * kBN) / p.kq];
-        const float c = __fmul_rn(__fmul_rn(qs, ks), p.scale);
-        const float smax = __fmul_rn(mx, c);
-        const float m_new = fmaxf(m, smax);
+        float mx[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mx[k] = fmaxf(__uint_as_float(r[2 * k]), __uint_as_float(r[2 * k + 1]));
+#pragma unroll
+        for (int t = 1; t < 8; ++t)
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+                mx[k] = fmax3(mx[k], __uint_as_float(r[16 * t + 2 * k]), __uint_as_float(r[16 * t + 2 * k + 1]));
+        const float rmax = fmaxf(fmax3(mx[0], mx[1], mx[2]), fmax3(fmax3(mx[3], mx[4], mx[5]), mx[6], mx[7]));
+        const float c = __fmul_rn(__fmul_rn(qs_scale, ks), p.scale);
+        const float m_new = fmaxf(m, __fmul_rn(rmax, c));
         const float alpha = expf(m - m_new);
         float A, Bc;
-        if (p.expcast) {
+        if (EXPCAST) {
             A = __fmul_rn(c, kC1);
             Bc = __fsub_rn(kC2, __fmul_rn(m_new, kC1));
-            const float umax = fmaf(mx, A, Bc);
+            const float umax = fmaf(rmax, A, Bc);
             if (umax > 120.25f) Bc = __fsub_rn(Bc, __fsub_rn(umax, kC2));
             A = __fmul_rn(A, kTwoM24);
             Bc = __fmul_rn(Bc, kTwoM24);
@@ -227,43 +247,45 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, vola
             A = __fmul_rn(c, kLog2e);
             Bc = __fsub_rn(8.0f, __fmul_rn(m_new, kLog2e));
         }
-        float psum = 0.0f;
+        const float2 AA = make_float2(A, A), BB = make_float2(Bc, Bc);
+        float ms[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        uint32_t pk[32];
 #pragma unroll
-        for (int ch = 0; ch < 4; ++ch) {
-            uint32_t r[32];
-            tmem_ld32(ts + 32 * ch, r);
-            tmem_wait_ld();
-            uint32_t pk[8];
-#pragma unroll
-            for (int w = 0; w < 8; ++w) {
-                float v[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    v[e] = __uint_as_float(r[4 * w + e]);
-                    if (tail && 32 * ch + 4 * w + e >= nvalid) v[e] = -INFINITY;
-                }
-                if (p.expcast) {
-                    const uint32_t h01 = cvt_relu_f16x2(fmaf(v[1], A, Bc), fmaf(v[0], A, Bc));
-                    const uint32_t h23 = cvt_relu_f16x2(fmaf(v[3], A, Bc), fmaf(v[2], A, Bc));
-                    pk[w] = __byte_perm(h01, h23, 0x6420);
-                } else {
-                    float e[4];
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        e[q] = exp2f(fmaf(v[q], A, Bc));
-                        psum = __fadd_rn(psum, e[q]);
-                    }
-                    pk[w] = e4m3x2(e[0], e[1]) | (e4m3x2(e[2], e[3]) << 16);
-                }
+        for (int w = 0; w < 32; ++w) {
+            const float2 g01 = ffma2(make_float2(__uint_as_float(r[4 * w]), __uint_as_float(r[4 * w + 1])), AA, BB);
+            const float2 g23 =
+                ffma2(make_float2(__uint_as_float(r[4 * w + 2]), __uint_as_float(r[4 * w + 3])), AA, BB);
+            if (EXPCAST) {
+                const uint32_t h01 = cvt_relu_f16x2(g01.y, g01.x);   // integer codes as f16 subnormals
+                const uint32_t h23 = cvt_relu_f16x2(g23.y, g23.x);
+                pk[w] = __byte_perm(h01, h23, 0x6420);
+                // code << 7 read as f16 is exactly decode(code) / 256
+                add_f16x2_to_f32(ms[0], ms[1], h01 << 7);
+                add_f16x2_to_f32(ms[2], ms[3], h23 << 7);
+            } else {
+                const float e0 = exp2f(g01.x), e1 = exp2f(g01.y), e2 = exp2f(g23.x), e3 = exp2f(g23.y);
+                ms[0] = __fadd_rn(ms[0], e0);
+                ms[1] = __fadd_rn(ms[1], e1);
+                ms[2] = __fadd_rn(ms[2], e2);
+                ms[3] = __fadd_rn(ms[3], e3);
+                pk[w] = e4m3x2(e0, e1) | (e4m3x2(e2, e3) << 16);
             }
-            tmem_st8(ts + 8 * ch, pk);
         }
-        tmem_wait_st();
+        // ExpCast: ms holds sum(p) = mass; scale to units of 256.  Otherwise
+        // ms already holds sum(p * 256).
+        float M = __fadd_rn(__fadd_rn(ms[0], ms[1]), __fadd_rn(ms[2], ms[3]));
+        if (EXPCAST) M = __fmul_rn(M, 256.0f);
+        if (j >= 2 && !mbar_wait(&B.o_full[b], ((j - 2) >> 1) & 1, abort)) break;   // P buffer free
+        uint8_t* prow = prow_base + b * kTile;
+#pragma unroll
+        for (int c16 = 0; c16 < 8; ++c16)
+            *reinterpret_cast<uint4*>(prow + (((uint32_t)c16 ^ swz) << 4)) =
+                make_uint4(pk[4 * c16], pk[4 * c16 + 1], pk[4 * c16 + 2], pk[4 * c16 + 3]);
+        fence_proxy_async_smem();
         const int slot = j & 3;
         if (j >= 4 && !mbar_wait(&B.st_free[slot], ((j >> 2) - 1) & 1, abort)) break;
         st_alpha[slot * 128 + row] = alpha;
-        st_mass[slot * 128 + row] = psum;
-        tc_fence_before();
+        st_mass[slot * 128 + row] = M;
         __syncwarp();
         if (lane == 0) {
             mbar_arrive(&B.p_full[b]);
@@ -273,6 +295,7 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, vola
     }
 }
 
+template <bool HAS_MEAN>
 __device__ void correction_role(const Params& p, uint8_t* smem, const Bars& B, volatile int* abort,
                                 uint32_t tmem, int qtile, int head, int quarter, int half, int lane) {
     const int row = quarter * 32 + lane;
@@ -280,52 +303,53 @@ __device__ void correction_role(const Params& p, uint8_t* smem, const Bars& B, v
     const float* st_mass = st_alpha + 4 * 128;
     const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
     const int c0 = half * 64;
-    float acc[64];
+    float2 acc[32];
 #pragma unroll
-    for (int i = 0; i < 64; ++i) acc[i] = 0.0f;
+    for (int i = 0; i < 32; ++i) acc[i] = make_float2(0.0f, 0.0f);
     float den = 0.0f;
     bool done = true;
     for (int j = 0; j < p.T; ++j) {
-        if (!mbar_wait(B.o_full, j & 1, abort)) { done = false; break; }
-        const int slot = j & 3, sp = j % kStages;
-        if (!mbar_wait(&B.st_full[slot], (j >> 2) & 1, abort)) { done = false; break; }
+        const int b = j & 1, slot = j & 3, s = j % kStages;
+        if (!mbar_wait(&B.o_full[b], (j >> 1) & 1, abort) ||
+            !mbar_wait(&B.st_full[slot], (j >> 2) & 1, abort)) {
+            done = false;
+            break;
+        }
         tc_fence_after();
+        uint32_t o[64];
+        const uint32_t to = trow + kColO + b * 128 + c0;
+        tmem_ld32_at<0>(to, o);
+        tmem_ld32_at<32>(to + 32, o);
+        tmem_wait_ld();
+        tc_fence_before();
         const float alpha = st_alpha[slot * 128 + row];
-        float M = st_mass[slot * 128 + row];
-        const float* meta = reinterpret_cast<const float*>(smem + kOffStages + sp * kStageBytes + kTile + kVBytes);
+        const float M = st_mass[slot * 128 + row];
+        __syncwarp();
+        if (lane == 0) {
+            mbar_arrive(&B.o_free[b]);
+            mbar_arrive(&B.st_free[slot]);
+        }
+        const float4* meta = reinterpret_cast<const float4*>(smem + kOffStages + s * kStageBytes + 2 * kTile);
         const bool rescale = __any_sync(0xffffffffu, alpha != 1.0f);
+        const float2 aa = make_float2(alpha, alpha), MM = make_float2(M, M);
 #pragma unroll
-        for (int ch = 0; ch < 2; ++ch) {
-            uint32_t r[32];
-            tmem_ld32(trow + kColO + c0 + 32 * ch, r);
-            if (ch == 0 && p.expcast) {
-                uint32_t mu;
-                tmem_ld1(trow + kColO + 128, mu);
-                tmem_wait_ld();
-                M = __uint_as_float(mu);
-            } else {
-                tmem_wait_ld();
-            }
-            if (ch == 1) {
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(B.o_free);
-            }
+        for (int q = 0; q < 16; ++q) {
+            const float4 vs = meta[(c0 >> 2) + q];
+            float4 mu = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (HAS_MEAN) mu = meta[32 + (c0 >> 2) + q];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                const int col = c0 + 32 * ch + i;
-                const float o = __uint_as_float(r[i]);
-                const float x = p.has_mean ? fmaf(M, meta[128 + col], o) : o;
-                const float a = rescale ? __fmul_rn(acc[32 * ch + i], alpha) : acc[32 * ch + i];
-                acc[32 * ch + i] = fmaf(x, meta[col], a);
+            for (int h = 0; h < 2; ++h) {
+                const int i = 2 * q + h;
+                float2 x = make_float2(__uint_as_float(o[2 * i]), __uint_as_float(o[2 * i + 1]));
+                const float2 v2 = h ? make_float2(vs.z, vs.w) : make_float2(vs.x, vs.y);
+                if (HAS_MEAN) x = ffma2(MM, h ? make_float2(mu.z, mu.w) : make_float2(mu.x, mu.y), x);
+                const float2 a = rescale ? fmul2(acc[i], aa) : acc[i];
+                acc[i] = ffma2(x, v2, a);
             }
         }
         den = __fadd_rn(__fmul_rn(alpha, den), M);
         __syncwarp();
-        if (lane == 0) {
-            mbar_arrive(&B.st_free[slot]);
-            mbar_arrive(&B.kv_empty[sp]);
-        }
+        if (lane == 0) mbar_arrive(&B.kv_empty[s]);
     }
     if (!done) return;
     const int64_t grow = (int64_t)qtile * kBM + row;
@@ -338,9 +362,9 @@ __device__ void correction_role(const Params& p, uint8_t* smem, const Bars& B, v
             uint32_t w[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                __nv_bfloat162 h = __floats2bfloat162_rn(__fdiv_rn(acc[8 * q + 2 * e], den),
-                                                         __fdiv_rn(acc[8 * q + 2 * e + 1], den));
-                w[e] = *reinterpret_cast<uint32_t*>(&h);
+                const float2 a = acc[4 * q + e];
+                __nv_bfloat162 h2 = __floats2bfloat162_rn(__fdiv_rn(a.x, den), __fdiv_rn(a.y, den));
+                w[e] = *reinterpret_cast<uint32_t*>(&h2);
             }
             dst[q] = make_uint4(w[0], w[1], w[2], w[3]);
         }
@@ -350,13 +374,14 @@ __device__ void correction_role(const Params& p, uint8_t* smem, const Bars& B, v
     for (int i = 0; i < 64; ++i) {
         const int col = c0 + i;
         if (col >= p.dv) break;
-        const float val = __fdiv_rn(acc[i], den);
+        const float val = __fdiv_rn((i & 1) ? acc[i >> 1].y : acc[i >> 1].x, den);
         if (p.out_dtype == VCB_BF16) static_cast<__nv_bfloat16*>(p.out)[base + col] = __float2bfloat16_rn(val);
         else if (p.out_dtype == VCB_F16) static_cast<__half*>(p.out)[base + col] = __float2half_rn(val);
         else static_cast<float*>(p.out)[base + col] = val;
     }
 }
 
+template <bool EXPCAST, bool HAS_MEAN>
 __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant__ Params p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -374,10 +399,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&B.s_full[b], 1);
-            mbar_init(&B.p_full[b], 4);           // 4 softmax warps
+            mbar_init(&B.s_free[b], 4);           // 4 softmax warps
+            mbar_init(&B.p_full[b], 4);
+            mbar_init(&B.o_full[b], 1);
+            mbar_init(&B.o_free[b], 8);           // 8 correction warps
         }
-        mbar_init(B.o_full, 1);
-        mbar_init(B.o_free, 8);
         for (int s = 0; s < 4; ++s) {
             mbar_init(&B.st_full[s], 4);
             mbar_init(&B.st_free[s], 8);
@@ -386,13 +412,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
         *abort = 0;
         fence_barrier_init();
     }
-    // rows 128..143 of every V buffer: E4M3 1.0, the ones that make O[:,128] the row mass
-    for (int i = threadIdx.x; i < kStages * 128; i += kThreads) {
-        const int s = i / 128, q = i % 128;
-        reinterpret_cast<uint4*>(smem + kOffStages + s * kStageBytes + kTile + kTile)[q] =
-            make_uint4(0x38383838u, 0x38383838u, 0x38383838u, 0x38383838u);
-    }
-    fence_proxy_async_smem();
     if (warp == 1) {
         tmem_alloc(tmem_slot, kTmemCols);
         tmem_relinquish();
@@ -402,14 +421,16 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 0) {
-        if (lane == 0) producer(p, smem, B, abort, qtile, head);
-    } else if (warp == 1) {
-        if (lane == 0) mma_issuer(p, smem, B, abort, tmem);
-    } else if (warp >= 4 && warp < 8) {
-        softmax_role(p, smem, B, abort, tmem, qtile, head, warp - 4, lane);
-    } else if (warp >= 8) {
-        correction_role(p, smem, B, abort, tmem, qtile, head, warp & 3, (warp - 8) >> 2, lane);
+    if (warp < 4) {
+        reg_dealloc<40>();
+        if (warp == 0 && lane == 0) producer(p, smem, B, abort, qtile, head);
+        if (warp == 1 && lane == 0) mma_issuer(p, smem, B, abort, tmem);
+    } else if (warp < 8) {
+        reg_alloc<168>();
+        softmax_role<EXPCAST>(p, smem, B, abort, tmem, qtile, head, warp - 4, lane);
+    } else {
+        reg_alloc<152>();
+        correction_role<HAS_MEAN>(p, smem, B, abort, tmem, qtile, head, warp & 3, (warp - 8) >> 2, lane);
     }
     tc_fence_before();
     __syncthreads();
@@ -454,6 +475,14 @@ int make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t planes)
     return VCB_OK;
 }
 
+template <bool E, bool M>
+int launch(const Params& p, dim3 grid, cudaStream_t st) {
+    VCB_CUDA(cudaFuncSetAttribute(attn_kernel<E, M>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemAlloc));
+    attn_kernel<E, M><<<grid, kThreads, kSmemAlloc, st>>>(p);
+    VCB_CUDA(cudaGetLastError());
+    return VCB_OK;
+}
+
 }  // namespace
 
 int attn_run(const vcb_attn_args* a, cudaStream_t st) {
@@ -479,15 +508,11 @@ int attn_run(const vcb_attn_args* a, cudaStream_t st) {
     p.nqb = (int)((a->sq + a->q_block - 1) / a->q_block);
     p.nkb = (int)((a->sk + a->k_quant_block - 1) / a->k_quant_block);
     p.T = T;
-    p.expcast = a->expcast;
-    p.has_mean = a->has_mean;
     p.out_dtype = a->out_dtype;
     p.scale = a->scale;
-    VCB_CUDA(cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemAlloc));
     const dim3 grid((unsigned)((a->sq + kBM - 1) / kBM), (unsigned)a->heads);
-    attn_kernel<<<grid, kThreads, kSmemAlloc, st>>>(p);
-    VCB_CUDA(cudaGetLastError());
-    return VCB_OK;
+    if (a->expcast) return a->has_mean ? launch<true, true>(p, grid, st) : launch<true, false>(p, grid, st);
+    return a->has_mean ? launch<false, true>(p, grid, st) : launch<false, false>(p, grid, st);
 }
 
 }  // namespace vcb

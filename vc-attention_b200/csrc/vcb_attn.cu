@@ -42,16 +42,17 @@ namespace {
 constexpr int kBM = 128;
 constexpr int kBN = 128;
 constexpr int kStages = 4;
-constexpr int kThreads = 512;
+constexpr int kThreads = 640;                    // 20 warps: 4 producer/MMA, 8 softmax, 8 correction
 constexpr uint32_t kTile = 128 * 128;            // one E4M3 tile (16 KB)
 constexpr uint32_t kMetaBytes = 1024;            // vscale[128], mu[128]
 constexpr uint32_t kStageBytes = 2 * kTile + kMetaBytes;
 constexpr uint32_t kOffQ = 0;
 constexpr uint32_t kOffP = kTile;                // P0, P1
 constexpr uint32_t kOffStages = kOffP + 2 * kTile;
-constexpr uint32_t kOffStats = kOffStages + kStages * kStageBytes;   // alpha[4][128], mass[4][128]
-constexpr uint32_t kOffBars = kOffStats + 2 * 4 * 128 * 4;
-constexpr int kNumBars = 1 + 2 * kStages + 2 * 5 + 2 * 4 + 1;
+constexpr uint32_t kOffStats = kOffStages + kStages * kStageBytes;   // alpha[4][128], mass[4][2][128]
+constexpr uint32_t kOffXmax = kOffStats + 3 * 4 * 128 * 4;            // partial row max [2][2][128]
+constexpr uint32_t kOffBars = kOffXmax + 2 * 2 * 128 * 4;
+constexpr int kNumBars = 1 + 2 * kStages + 2 * 5 + 2 * 4 + 1 + 8;
 constexpr uint32_t kOffMisc = kOffBars + kNumBars * 8;
 constexpr uint32_t kSmemBytes = kOffMisc + 16;
 constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;
@@ -89,6 +90,7 @@ struct Bars {
     uint64_t* st_full;     // [4]  alpha / mass of tile j
     uint64_t* st_free;     // [4]
     uint64_t* drain;
+    uint64_t* xmax;        // [4 quarters][2]  the two softmax halves of a row exchanged their maxima
 };
 
 __device__ __forceinline__ Bars bars_at(uint8_t* smem) {
@@ -104,7 +106,8 @@ __device__ __forceinline__ Bars bars_at(uint8_t* smem) {
     r.o_free = b; b += 2;
     r.st_full = b; b += 4;
     r.st_free = b; b += 4;
-    r.drain = b;
+    r.drain = b; b += 1;
+    r.xmax = b;
     return r;
 }
 
@@ -187,18 +190,23 @@ __device__ void mma_issuer(const Params& p, uint8_t* smem, const Bars& B, volati
     drain_wait(B.drain, 0);
 }
 
+// Two threads per query row: warps 4-7 own columns [0, 64) of the S tile,
+// warps 8-11 columns [64, 128), each warp the TMEM lane quarter warp % 4.
+// The halves exchange their partial row maxima through shared memory and a
+// per-quarter mbarrier (bounded wait, so a timed-out partner cannot hang it).
 template <bool EXPCAST>
 __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, volatile int* abort, uint32_t tmem,
-                             int qtile, int head, int quarter, int lane) {
+                             int qtile, int head, int quarter, int hs, int lane) {
     const int row = quarter * 32 + lane;
     const int64_t grow = (int64_t)qtile * kBM + row;
     int qb = (int)(grow / p.q_block);
     if (qb >= p.nqb) qb = p.nqb - 1;
-    const float qs_scale = __fmul_rn(p.q_scale[(int64_t)head * p.nqb + qb], 1.0f);
+    const float qs_scale = p.q_scale[(int64_t)head * p.nqb + qb];
     const float* ksp = p.k_scale + (int64_t)head * p.nkb;
     float* st_alpha = reinterpret_cast<float*>(smem + kOffStats);
-    float* st_mass = st_alpha + 4 * 128;
-    const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
+    float* st_mass = st_alpha + 4 * 128;                       // [4][2][128]
+    float* xmax = reinterpret_cast<float*>(smem + kOffXmax);   // [2][2][128]
+    const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16) + 64 * hs;
     uint8_t* prow_base = smem + kOffP + row * 128;
     const uint32_t swz = (uint32_t)(row & 7);
     float m = -INFINITY;
@@ -207,31 +215,34 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, vola
         const float ks = __ldg(ksp + ((int64_t)j * kBN) / p.kq);
         if (!mbar_wait(&B.s_full[b], (j >> 1) & 1, abort)) break;
         tc_fence_after();
-        uint32_t r[128];
+        uint32_t r[64];
         const uint32_t ts = trow + kColS + b * kBN;
         tmem_ld32_at<0>(ts, r);
         tmem_ld32_at<32>(ts + 32, r);
-        tmem_ld32_at<64>(ts + 64, r);
-        tmem_ld32_at<96>(ts + 96, r);
         tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&B.s_free[b]);
-        const int nvalid = (int)min((int64_t)kBN, p.sk - (int64_t)j * kBN);
-        if (nvalid < kBN) {
+        const int nvalid = (int)min((int64_t)kBN, p.sk - (int64_t)j * kBN) - 64 * hs;
+        if (nvalid < 64) {
 #pragma unroll
-            for (int i = 0; i < 128; ++i)
+            for (int i = 0; i < 64; ++i)
                 if (i >= nvalid) r[i] = 0xff800000u;   // -inf: masked key
         }
-        float mx[8];
+        float mx[4];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) mx[k] = fmaxf(__uint_as_float(r[2 * k]), __uint_as_float(r[2 * k + 1]));
+        for (int k = 0; k < 4; ++k) mx[k] = fmaxf(__uint_as_float(r[2 * k]), __uint_as_float(r[2 * k + 1]));
 #pragma unroll
         for (int t = 1; t < 8; ++t)
 #pragma unroll
-            for (int k = 0; k < 8; ++k)
-                mx[k] = fmax3(mx[k], __uint_as_float(r[16 * t + 2 * k]), __uint_as_float(r[16 * t + 2 * k + 1]));
-        const float rmax = fmaxf(fmax3(mx[0], mx[1], mx[2]), fmax3(fmax3(mx[3], mx[4], mx[5]), mx[6], mx[7]));
+            for (int k = 0; k < 4; ++k)
+                mx[k] = fmax3(mx[k], __uint_as_float(r[8 * t + 2 * k]), __uint_as_float(r[8 * t + 2 * k + 1]));
+        const float pmax = fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]);
+        xmax[(b * 2 + hs) * 128 + row] = pmax;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&B.xmax[quarter * 2 + b]);
+        if (!mbar_wait(&B.xmax[quarter * 2 + b], (j >> 1) & 1, abort)) break;
+        const float rmax = fmaxf(pmax, xmax[(b * 2 + (hs ^ 1)) * 128 + row]);
         const float c = __fmul_rn(__fmul_rn(qs_scale, ks), p.scale);
         const float m_new = fmaxf(m, __fmul_rn(rmax, c));
         const float alpha = expf(m - m_new);
@@ -249,9 +260,9 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, vola
         }
         const float2 AA = make_float2(A, A), BB = make_float2(Bc, Bc);
         float ms[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        uint32_t pk[32];
+        uint32_t pk[16];
 #pragma unroll
-        for (int w = 0; w < 32; ++w) {
+        for (int w = 0; w < 16; ++w) {
             const float2 g01 = ffma2(make_float2(__uint_as_float(r[4 * w]), __uint_as_float(r[4 * w + 1])), AA, BB);
             const float2 g23 =
                 ffma2(make_float2(__uint_as_float(r[4 * w + 2]), __uint_as_float(r[4 * w + 3])), AA, BB);
@@ -278,14 +289,14 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, vola
         if (j >= 2 && !mbar_wait(&B.o_full[b], ((j - 2) >> 1) & 1, abort)) break;   // P buffer free
         uint8_t* prow = prow_base + b * kTile;
 #pragma unroll
-        for (int c16 = 0; c16 < 8; ++c16)
-            *reinterpret_cast<uint4*>(prow + (((uint32_t)c16 ^ swz) << 4)) =
-                make_uint4(pk[4 * c16], pk[4 * c16 + 1], pk[4 * c16 + 2], pk[4 * c16 + 3]);
+        for (int c = 0; c < 4; ++c)
+            *reinterpret_cast<uint4*>(prow + (((uint32_t)(4 * hs + c) ^ swz) << 4)) =
+                make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
         fence_proxy_async_smem();
         const int slot = j & 3;
         if (j >= 4 && !mbar_wait(&B.st_free[slot], ((j >> 2) - 1) & 1, abort)) break;
-        st_alpha[slot * 128 + row] = alpha;
-        st_mass[slot * 128 + row] = M;
+        if (hs == 0) st_alpha[slot * 128 + row] = alpha;
+        st_mass[(slot * 2 + hs) * 128 + row] = M;
         __syncwarp();
         if (lane == 0) {
             mbar_arrive(&B.p_full[b]);
@@ -300,7 +311,7 @@ __device__ void correction_role(const Params& p, uint8_t* smem, const Bars& B, v
                                 uint32_t tmem, int qtile, int head, int quarter, int half, int lane) {
     const int row = quarter * 32 + lane;
     const float* st_alpha = reinterpret_cast<const float*>(smem + kOffStats);
-    const float* st_mass = st_alpha + 4 * 128;
+    const float* st_mass = st_alpha + 4 * 128;          // [4][2][128]
     const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
     const int c0 = half * 64;
     float2 acc[32];
@@ -316,35 +327,39 @@ __device__ void correction_role(const Params& p, uint8_t* smem, const Bars& B, v
             break;
         }
         tc_fence_after();
-        uint32_t o[64];
-        const uint32_t to = trow + kColO + b * 128 + c0;
-        tmem_ld32_at<0>(to, o);
-        tmem_ld32_at<32>(to + 32, o);
-        tmem_wait_ld();
-        tc_fence_before();
         const float alpha = st_alpha[slot * 128 + row];
-        const float M = st_mass[slot * 128 + row];
+        const float M = __fadd_rn(st_mass[(slot * 2) * 128 + row], st_mass[(slot * 2 + 1) * 128 + row]);
         __syncwarp();
-        if (lane == 0) {
-            mbar_arrive(&B.o_free[b]);
-            mbar_arrive(&B.st_free[slot]);
-        }
+        if (lane == 0) mbar_arrive(&B.st_free[slot]);
         const float4* meta = reinterpret_cast<const float4*>(smem + kOffStages + s * kStageBytes + 2 * kTile);
         const bool rescale = __any_sync(0xffffffffu, alpha != 1.0f);
         const float2 aa = make_float2(alpha, alpha), MM = make_float2(M, M);
+        const uint32_t to = trow + kColO + b * 128 + c0;
 #pragma unroll
-        for (int q = 0; q < 16; ++q) {
-            const float4 vs = meta[(c0 >> 2) + q];
-            float4 mu = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (HAS_MEAN) mu = meta[32 + (c0 >> 2) + q];
+        for (int ch = 0; ch < 2; ++ch) {
+            uint32_t o[32];
+            tmem_ld32_at<0>(to + 32 * ch, o);
+            tmem_wait_ld();
+            if (ch == 1) {
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&B.o_free[b]);
+            }
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const int i = 2 * q + h;
-                float2 x = make_float2(__uint_as_float(o[2 * i]), __uint_as_float(o[2 * i + 1]));
-                const float2 v2 = h ? make_float2(vs.z, vs.w) : make_float2(vs.x, vs.y);
-                if (HAS_MEAN) x = ffma2(MM, h ? make_float2(mu.z, mu.w) : make_float2(mu.x, mu.y), x);
-                const float2 a = rescale ? fmul2(acc[i], aa) : acc[i];
-                acc[i] = ffma2(x, v2, a);
+            for (int q = 0; q < 8; ++q) {
+                const float4 vs = meta[(c0 >> 2) + 8 * ch + q];
+                float4 mu = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (HAS_MEAN) mu = meta[32 + (c0 >> 2) + 8 * ch + q];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int i = 16 * ch + 2 * q + h;
+                    const int k = 4 * q + 2 * h;
+                    float2 x = make_float2(__uint_as_float(o[k]), __uint_as_float(o[k + 1]));
+                    const float2 v2 = h ? make_float2(vs.z, vs.w) : make_float2(vs.x, vs.y);
+                    if (HAS_MEAN) x = ffma2(MM, h ? make_float2(mu.z, mu.w) : make_float2(mu.x, mu.y), x);
+                    const float2 a = rescale ? fmul2(acc[i], aa) : acc[i];
+                    acc[i] = ffma2(x, v2, a);
+                }
             }
         }
         den = __fadd_rn(__fmul_rn(alpha, den), M);
@@ -399,16 +414,17 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&B.s_full[b], 1);
-            mbar_init(&B.s_free[b], 4);           // 4 softmax warps
-            mbar_init(&B.p_full[b], 4);
+            mbar_init(&B.s_free[b], 8);           // 8 softmax warps
+            mbar_init(&B.p_full[b], 8);
             mbar_init(&B.o_full[b], 1);
             mbar_init(&B.o_free[b], 8);           // 8 correction warps
         }
         for (int s = 0; s < 4; ++s) {
-            mbar_init(&B.st_full[s], 4);
+            mbar_init(&B.st_full[s], 8);
             mbar_init(&B.st_free[s], 8);
         }
         mbar_init(B.drain, 1);
+        for (int i = 0; i < 8; ++i) mbar_init(&B.xmax[i], 2);   // the two softmax warps of a quarter
         *abort = 0;
         fence_barrier_init();
     }
@@ -421,16 +437,18 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    // Register split of the 640 x 96 launch budget: producer/MMA group 32,
+    // softmax groups 96 (unchanged), correction groups 120; 4096 + 24576 +
+    // 30720 = 59392 <= 61440.
     if (warp < 4) {
-        reg_dealloc<40>();
+        reg_dealloc<32>();
         if (warp == 0 && lane == 0) producer(p, smem, B, abort, qtile, head);
         if (warp == 1 && lane == 0) mma_issuer(p, smem, B, abort, tmem);
-    } else if (warp < 8) {
-        reg_alloc<168>();
-        softmax_role<EXPCAST>(p, smem, B, abort, tmem, qtile, head, warp - 4, lane);
+    } else if (warp < 12) {
+        softmax_role<EXPCAST>(p, smem, B, abort, tmem, qtile, head, warp & 3, (warp - 4) >> 2, lane);
     } else {
-        reg_alloc<152>();
-        correction_role<HAS_MEAN>(p, smem, B, abort, tmem, qtile, head, warp & 3, (warp - 8) >> 2, lane);
+        reg_alloc<120>();
+        correction_role<HAS_MEAN>(p, smem, B, abort, tmem, qtile, head, warp & 3, (warp - 12) >> 2, lane);
     }
     tc_fence_before();
     __syncthreads();

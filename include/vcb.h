@@ -45,7 +45,8 @@ enum vcb_dtype { VCB_F32 = 0, VCB_F16 = 1, VCB_BF16 = 2 };
 /* Bits of the device status word that kernels set (see vcb_read_status). */
 enum vcb_device_flags {
     VCB_FLAG_NONFINITE = 1,         /* a Q, K or V element was NaN or Inf */
-    VCB_FLAG_TIMEOUT = 2            /* a bounded wait in the attention kernel expired */
+    VCB_FLAG_TIMEOUT = 2,           /* a bounded wait in the attention kernel expired */
+    VCB_FLAG_INTERNAL = 4           /* a device-side layout check failed; nothing was computed */
 };
 
 /* ---- identification --------------------------------------------------- */

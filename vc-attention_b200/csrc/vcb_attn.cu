@@ -115,7 +115,7 @@ __device__ __forceinline__ Bars bars_at(uint8_t* smem) {
 __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
     const uint32_t a = smem_u32(bar);
     const uint64_t t0 = globaltimer();
-    while (!mbar_try_wait(a, parity)) {
+    while (!mbar_try_wait_sleep(a, parity, kSuspendHintNs)) {
         if (globaltimer() - t0 > kWaitLimitNs) return;
     }
 }
@@ -133,8 +133,8 @@ __device__ void producer(const Params& p, uint8_t* smem, const Bars& B, volatile
     prefetch_tmap(&p.tm_v);
     mbar_arrive_expect_tx(B.q_full, kTile);
     tma_load_3d(smem + kOffQ, &p.tm_q, B.q_full, 0, qtile * kBM, head);
-    int armed[kStages] = {0, 0, 0, 0};
     const float* meta = p.v_meta + (int64_t)head * p.T * 256;
+    int loaded = 0;
     for (int j = 0; j < p.T; ++j) {
         const int s = j % kStages, u = j / kStages;
         if (u > 0 && !mbar_wait(&B.kv_empty[s], (u - 1) & 1, abort)) break;
@@ -143,12 +143,12 @@ __device__ void producer(const Params& p, uint8_t* smem, const Bars& B, volatile
         tma_load_3d(st, &p.tm_k, &B.kv_full[s], 0, j * kBN, head);
         tma_load_3d(st + kTile, &p.tm_v, &B.kv_full[s], 0, j * 128, head);
         bulk_load(st + 2 * kTile, meta + (int64_t)j * 256, kMetaBytes, &B.kv_full[s]);
-        armed[s] = u + 1;
+        loaded = j + 1;
     }
     if (*abort) {   // no TMA write may land after the CTA exits
         drain_wait(B.q_full, 0);
-        for (int s = 0; s < kStages; ++s)
-            if (armed[s] > 0) drain_wait(&B.kv_full[s], (armed[s] - 1) & 1);
+        for (int s = 0; s < kStages && s < loaded; ++s)     // last use of stage s: tile s + 4 u
+            drain_wait(&B.kv_full[s], ((loaded - 1 - s) / kStages) & 1);
     }
 }
 
@@ -209,10 +209,16 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, vola
     const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16) + 64 * hs;
     uint8_t* prow_base = smem + kOffP + row * 128;
     const uint32_t swz = (uint32_t)(row & 7);
+    const int kstep = p.kq / kBN;
+    int kidx = 0, kcnt = 0;
     float m = -INFINITY;
     for (int j = 0; j < p.T; ++j) {
         const int b = j & 1;
-        const float ks = __ldg(ksp + ((int64_t)j * kBN) / p.kq);
+        const float ks = __ldg(ksp + kidx);
+        if (++kcnt == kstep) {          // K scale block changes every kq / 128 tiles
+            kcnt = 0;
+            ++kidx;
+        }
         if (!mbar_wait(&B.s_full[b], (j >> 1) & 1, abort)) break;
         tc_fence_after();
         uint32_t r[64];
@@ -222,7 +228,7 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, vola
         tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&B.s_free[b]);
+        mbar_arrive_if(&B.s_free[b], lane == 0);
         const int nvalid = (int)min((int64_t)kBN, p.sk - (int64_t)j * kBN) - 64 * hs;
         if (nvalid < 64) {
 #pragma unroll
@@ -240,7 +246,7 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, vola
         const float pmax = fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]);
         xmax[(b * 2 + hs) * 128 + row] = pmax;
         __syncwarp();
-        if (lane == 0) mbar_arrive(&B.xmax[quarter * 2 + b]);
+        mbar_arrive_if(&B.xmax[quarter * 2 + b], lane == 0);
         if (!mbar_wait(&B.xmax[quarter * 2 + b], (j >> 1) & 1, abort)) break;
         const float rmax = fmaxf(pmax, xmax[(b * 2 + (hs ^ 1)) * 128 + row]);
         const float c = __fmul_rn(__fmul_rn(qs_scale, ks), p.scale);
@@ -298,10 +304,8 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, vola
         if (hs == 0) st_alpha[slot * 128 + row] = alpha;
         st_mass[(slot * 2 + hs) * 128 + row] = M;
         __syncwarp();
-        if (lane == 0) {
-            mbar_arrive(&B.p_full[b]);
-            mbar_arrive(&B.st_full[slot]);
-        }
+        mbar_arrive_if(&B.p_full[b], lane == 0);
+        mbar_arrive_if(&B.st_full[slot], lane == 0);
         m = m_new;
     }
 }
@@ -330,7 +334,7 @@ __device__ void correction_role(const Params& p, uint8_t* smem, const Bars& B, v
         const float alpha = st_alpha[slot * 128 + row];
         const float M = __fadd_rn(st_mass[(slot * 2) * 128 + row], st_mass[(slot * 2 + 1) * 128 + row]);
         __syncwarp();
-        if (lane == 0) mbar_arrive(&B.st_free[slot]);
+        mbar_arrive_if(&B.st_free[slot], lane == 0);
         const float4* meta = reinterpret_cast<const float4*>(smem + kOffStages + s * kStageBytes + 2 * kTile);
         const bool rescale = __any_sync(0xffffffffu, alpha != 1.0f);
         const float2 aa = make_float2(alpha, alpha), MM = make_float2(M, M);
@@ -343,7 +347,7 @@ __device__ void correction_role(const Params& p, uint8_t* smem, const Bars& B, v
             if (ch == 1) {
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&B.o_free[b]);
+                mbar_arrive_if(&B.o_free[b], lane == 0);
             }
 #pragma unroll
             for (int q = 0; q < 8; ++q) {
@@ -357,14 +361,14 @@ __device__ void correction_role(const Params& p, uint8_t* smem, const Bars& B, v
                     float2 x = make_float2(__uint_as_float(o[k]), __uint_as_float(o[k + 1]));
                     const float2 v2 = h ? make_float2(vs.z, vs.w) : make_float2(vs.x, vs.y);
                     if (HAS_MEAN) x = ffma2(MM, h ? make_float2(mu.z, mu.w) : make_float2(mu.x, mu.y), x);
-                    const float2 a = rescale ? fmul2(acc[i], aa) : acc[i];
-                    acc[i] = ffma2(x, v2, a);
+                    if (rescale) acc[i] = fmul2(acc[i], aa);      // warp-uniform
+                    acc[i] = ffma2(x, v2, acc[i]);
                 }
             }
         }
         den = __fadd_rn(__fmul_rn(alpha, den), M);
         __syncwarp();
-        if (lane == 0) mbar_arrive(&B.kv_empty[s]);
+        mbar_arrive_if(&B.kv_empty[s], lane == 0);
     }
     if (!done) return;
     const int64_t grow = (int64_t)qtile * kBM + row;
@@ -398,8 +402,14 @@ __device__ void correction_role(const Params& p, uint8_t* smem, const Bars& B, v
 
 template <bool EXPCAST, bool HAS_MEAN>
 __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant__ Params p) {
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // The swizzled TMA/MMA layouts need a 1024-byte aligned base; the kernel
+    // declares no static shared memory, so the dynamic window starts aligned.
+    // Checked anyway: a misaligned window reports an error and does nothing.
+    extern __shared__ __align__(1024) uint8_t smem[];
+    if (smem_u32(smem) & 1023u) {
+        if (threadIdx.x == 0) flag_status(p.status, VCB_FLAG_INTERNAL);
+        return;
+    }
     const Bars B = bars_at(smem);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffMisc);
     volatile int* abort = reinterpret_cast<volatile int*>(smem + kOffMisc + 4);

@@ -135,21 +135,35 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
-// A wait that gives up: after `limit_ns` of polling, or as soon as another
-// role has raised *abort, it returns false (and raises *abort itself on
-// timeout).  No wait in these kernels can spin forever.
+// try_wait with a suspend-time hint: a waiting warp is parked by the
+// hardware until the phase completes or about `hint_ns` pass, instead of
+// spinning and taking issue slots from the warps that do the work.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
+// A wait that gives up: after kWaitLimitNs, or as soon as another role has
+// raised *abort, it returns false (and raises *abort itself on timeout).  No
+// wait in these kernels can spin forever.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;   // 2 s, far above any real wait
+constexpr uint32_t kSuspendHintNs = 1000000u;      // re-check abort / deadline every ~1 ms
 
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
     const uint32_t a = smem_u32(bar);
-    if (mbar_try_wait(a, parity)) return true;
+    if (mbar_try_wait_sleep(a, parity, kSuspendHintNs)) return true;
     const uint64_t t0 = globaltimer();
-    for (uint32_t i = 1;; ++i) {
-        if (mbar_try_wait(a, parity)) return true;
-        if ((i & 63u) == 0) {
-            if (*abort) return false;
-            if (globaltimer() - t0 > kWaitLimitNs) { *abort = 1; return false; }
-        }
+    for (;;) {
+        if (mbar_try_wait_sleep(a, parity, kSuspendHintNs)) return true;
+        if (*abort) return false;
+        if (globaltimer() - t0 > kWaitLimitNs) { *abort = 1; return false; }
     }
 }
 
@@ -255,34 +269,20 @@ __device__ __forceinline__ void tmem_ld32_at(uint32_t taddr, uint32_t (&r)[N]) {
         : "r"(taddr));
 }
 
-// Packed FP32 pairs (sm_100): d = a * b + c, two lanes per instruction.
-__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
-    unsigned long long ra, rb, rc, rd;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(ra) : "f"(a.x), "f"(a.y));
-    asm("mov.b64 %0, {%1, %2};" : "=l"(rb) : "f"(b.x), "f"(b.y));
-    asm("mov.b64 %0, {%1, %2};" : "=l"(rc) : "f"(c.x), "f"(c.y));
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(rd) : "l"(ra), "l"(rb), "l"(rc));
-    float2 d;
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(d.x), "=f"(d.y) : "l"(rd));
-    return d;
-}
-__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
-    unsigned long long ra, rb, rd;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(ra) : "f"(a.x), "f"(a.y));
-    asm("mov.b64 %0, {%1, %2};" : "=l"(rb) : "f"(b.x), "f"(b.y));
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(rd) : "l"(ra), "l"(rb));
-    float2 d;
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(d.x), "=f"(d.y) : "l"(rd));
-    return d;
-}
-__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
-    unsigned long long ra, rb, rd;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(ra) : "f"(a.x), "f"(a.y));
-    asm("mov.b64 %0, {%1, %2};" : "=l"(rb) : "f"(b.x), "f"(b.y));
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(rd) : "l"(ra), "l"(rb));
-    float2 d;
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(d.x), "=f"(d.y) : "l"(rd));
-    return d;
+// Packed FP32 pairs (sm_100): two lanes per instruction, register pairing
+// left to the compiler.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+
+// mbarrier arrive by the lanes where `pred` holds, without a divergent branch.
+__device__ __forceinline__ void mbar_arrive_if(uint64_t* bar, bool pred) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "@p mbarrier.arrive.shared::cta.b64 _, [%0];\n\t}"
+        ::"r"(smem_u32(bar)), "r"((uint32_t)pred)
+        : "memory");
 }
 
 // Three-input maximum (sm_100).

@@ -23,6 +23,7 @@ VCB_ERR_WORKSPACE = 4
 VCB_F32, VCB_F16, VCB_BF16 = 0, 1, 2
 FLAG_NONFINITE = 1
 FLAG_TIMEOUT = 2
+FLAG_INTERNAL = 4
 
 c_int, c_int64, c_float, c_size_t, c_void_p = ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t, ctypes.c_void_p
 

@@ -152,6 +152,8 @@ def forward(q, k, v, cfg, *, pi, active, scale, out=None, workspace=None, status
                 raise ValueError("Q/K/V must be finite")
             if flags.value & _abi.FLAG_TIMEOUT:
                 raise RuntimeError("b200_fp8 attention kernel: a bounded device wait expired")
+            if flags.value & _abi.FLAG_INTERNAL:
+                raise RuntimeError("b200_fp8 attention kernel: device layout check failed")
     return out
 
 

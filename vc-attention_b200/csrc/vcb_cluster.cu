@@ -114,50 +114,69 @@ __global__ void __launch_bounds__(256) cluster_assign_kernel(ClusterArgs a) {
         a.labels[h * a.S + base + tid] = (uint8_t)best;
     }
     __syncthreads();
-    // Per-cluster partial sums in token order.  Thread (d, parity) owns
-    // clusters parity, parity + 2, ...; adding +0.0 for other tokens leaves
-    // every partial sum bit-identical to adding only the matching tokens.
-    const int d = tid & 127, parity = tid >> 7;
-    float acc[kMaxClusters / 2];
-#pragma unroll
-    for (int i = 0; i < kMaxClusters / 2; ++i) acc[i] = 0.0f;
+    // Stable order of the chunk's tokens by cluster (a counting sort): the
+    // rank of token j among earlier tokens of its cluster comes from warp
+    // match/ballot masks plus the per-warp counts of the warps before it.
+    __shared__ int wcnt[8][kMaxClusters];
+    __shared__ int seg[kMaxClusters + 1];
+    __shared__ uint16_t order[kChunk];
+    const int warp = tid >> 5, lane = tid & 31;
+    for (int i = tid; i < 8 * kMaxClusters; i += 256) (&wcnt[0][0])[i] = 0;
+    __syncthreads();
+    const int lj = tid < nvalid ? lab[tid] : -1;
+    const unsigned same = __match_any_sync(0xffffffffu, lj);
+    const int rank_in_warp = __popc(same & ((1u << lane) - 1u));
+    if (lj >= 0 && rank_in_warp == 0) wcnt[warp][lj] = __popc(same);
+    __syncthreads();
+    if (tid == 0) {
+        int run = 0;
+        for (int c = 0; c < count; ++c) {
+            seg[c] = run;
+            for (int w = 0; w < 8; ++w) run += wcnt[w][c];
+        }
+        seg[count] = run;
+    }
+    __syncthreads();
+    if (lj >= 0) {
+        int before = 0;
+        for (int w = 0; w < warp; ++w) before += wcnt[w][lj];
+        order[seg[lj] + before + rank_in_warp] = (uint16_t)tid;
+    }
+    __syncthreads();
+    // Per-cluster partial sums: each cluster's tokens in token order, the
+    // fixed order the CPU checker uses.  Threads 0..127 own clusters below
+    // count/2, threads 128..255 the rest; channel d = tid % 128.
+    const int d = tid & 127;
+    const int c_lo = tid < 128 ? 0 : count / 2, c_hi = tid < 128 ? count / 2 : count;
+    float* ps = a.psum + ((int64_t)h * a.nchunk + chunk) * count * 128;
     if (d < D) {
-        for (int j = 0; j < nvalid; ++j) {
-            const float val = Elem<T>::load(vh + (base + j) * D + d);
-            const int lj = lab[j];
-#pragma unroll
-            for (int i = 0; i < kMaxClusters / 2; ++i) {
-                const int c = parity + 2 * i;
-                if (c < count) acc[i] += (lj == c) ? val : 0.0f;
-            }
+        for (int c = c_lo; c < c_hi; ++c) {
+            float sum = 0.0f;
+            const int p1 = seg[c + 1];
+            for (int pos = seg[c]; pos < p1; ++pos) sum += Elem<T>::load(vh + (base + order[pos]) * D + d);
+            ps[c * 128 + d] = sum;
         }
     }
-    float* ps = a.psum + ((int64_t)h * a.nchunk + chunk) * count * 128;
-#pragma unroll
-    for (int i = 0; i < kMaxClusters / 2; ++i) {
-        const int c = parity + 2 * i;
-        if (c < count) ps[c * 128 + d] = acc[i];
-    }
-    if (tid < count) {
-        int n = 0;
-        for (int j = 0; j < nvalid; ++j) n += lab[j] == tid;
-        a.pcnt[((int64_t)h * a.nchunk + chunk) * count + tid] = n;
-    }
+    if (tid < count) a.pcnt[((int64_t)h * a.nchunk + chunk) * count + tid] = seg[tid + 1] - seg[tid];
 }
 
-__global__ void __launch_bounds__(256) cluster_update_kernel(ClusterArgs a) {
+// One CTA per (head, cluster), thread d per channel; chunks added in order
+// (the loads are independent, only the adds are chained).
+__global__ void __launch_bounds__(128) cluster_update_kernel(ClusterArgs a) {
     const int64_t h = blockIdx.x;
-    for (int i = threadIdx.x; i < a.count * 128; i += 256) {
-        const int c = i / 128, d = i % 128;
-        if (d >= a.D) continue;
-        float total = 0.0f;
-        long long n = 0;
-        for (int ch = 0; ch < a.nchunk; ++ch) {
-            total += a.psum[(((int64_t)h * a.nchunk + ch) * a.count + c) * 128 + d];
-            n += a.pcnt[((int64_t)h * a.nchunk + ch) * a.count + c];
-        }
-        if (n > 0) a.centers[(h * a.count + c) * a.D + d] = total / (float)n;
+    const int c = blockIdx.y, d = threadIdx.x;
+    if (d >= a.D) return;
+    const float* src = a.psum + ((int64_t)h * a.nchunk * a.count + c) * 128 + d;
+    const int32_t* cnt = a.pcnt + (int64_t)h * a.nchunk * a.count + c;
+    const int64_t stride = (int64_t)a.count * 128;
+    float total = 0.0f;
+    long long n = 0;
+#pragma unroll 8
+    for (int ch = 0; ch < a.nchunk; ++ch) {
+        total += __ldg(src + ch * stride);
+        n += __ldg(cnt + (int64_t)ch * a.count);
     }
+    if (n > 0) a.centers[(h * a.count + c) * a.D + d] = total / (float)n;
 }
 
 __global__ void cluster_offsets_kernel(ClusterArgs a) {
@@ -226,7 +245,7 @@ int run(const vcb_group_args* p, cudaStream_t st) {
     for (int it = 0; it < p->iterations; ++it) {
         cluster_assign_kernel<T><<<dim3(nchunk, (unsigned)p->heads), 256, 0, st>>>(a);
         VCB_CUDA(cudaGetLastError());
-        cluster_update_kernel<<<(unsigned)p->heads, 256, 0, st>>>(a);
+        cluster_update_kernel<<<dim3((unsigned)p->heads, (unsigned)count), 128, 0, st>>>(a);
         VCB_CUDA(cudaGetLastError());
     }
     cluster_offsets_kernel<<<(unsigned)p->heads, 32, 0, st>>>(a);

@@ -99,6 +99,18 @@ VCB_API int vcb_preprocess_qk(const vcb_qk_args* args, void* stream);
  * kernels.cu:72-120, launched at kernels.cu:307-310): writes q8/k8/scales */
 VCB_API int vcb_quantize_qk(const vcb_qk_args* args, void* stream);
 
+/* Same work and outputs as vcb_quantize_qk, for callers that cannot allocate
+ * device memory (for example a runtime's plugin enqueue hook, where the
+ * runtime has planned all device memory and a cudaMalloc would synchronise
+ * the device).  args->workspace is ignored: the K-mean scratch comes from a
+ * fixed 8 MiB array inside libvcb.so, held on every GPU that loads the
+ * library.  Calls needing more than 8 MiB (heads * (1 + ceil(sk / 256)) * 512
+ * bytes with k_smooth) fail with VCB_ERR_INVALID_ARGUMENT.  All calls share
+ * the array, so calls that overlap on the GPU race.  The first call on a
+ * device looks up the array's address and should come before any stream
+ * capture.  This entry point has no counterpart in the reference. */
+VCB_API int vcb_quantize_qk_static(const vcb_qk_args* args, void* stream);
+
 /* ---- V clustering (Lloyd + stable permutation) ---------------------------- */
 typedef struct {
     const void* v;          /* [heads, s, d] dtype */

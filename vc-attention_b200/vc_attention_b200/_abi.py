@@ -77,6 +77,7 @@ SIGNATURES = {
     "vcb_qk_workspace": (c_size_t, [c_int64, c_int64]),
     "vcb_preprocess_qk": (c_int, [ctypes.POINTER(QKArgs), c_void_p]),
     "vcb_quantize_qk": (c_int, [ctypes.POINTER(QKArgs), c_void_p]),
+    "vcb_quantize_qk_static": (c_int, [ctypes.POINTER(QKArgs), c_void_p]),
     "vcb_group_workspace": (c_size_t, [c_int64, c_int64, c_int, c_int]),
     "vcb_group_values": (c_int, [ctypes.POINTER(GroupArgs), c_void_p]),
     "vcb_prepare_v": (c_int, [ctypes.POINTER(VArgs), c_void_p]),

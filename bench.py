@@ -6,12 +6,13 @@ One step = one full forward of the hot path over one batch on each GPU:
 Lloyd clustering of V (a refresh step), Q/K demean + Hadamard + E4M3 block
 quantisation, V tiles, and the fused tcgen05 attention; B=1, H=40, S=32768,
 D=128, bf16 inputs, combined mode (ExpCast + V-Smooth), step 0 of 50.  With
-N GPUs (torchrun) every rank runs its own batch (weak scaling; global batch
-N), heads are independent so no collective touches the data path.
+N GPUs (torchrun) the 40 heads are split into contiguous ranges, 40/N per
+rank (strong scaling: configuration 3 shards 5 heads per GPU at N=8); heads
+are independent, so no collective touches the data path.
 
-value     FP8 attention TFLOPS, 4*B*H*S^2*D per step, summed over ranks, from
-          CUDA-event time of the step with inputs resident in HBM (max over
-          ranks).  Q/K/V (1 GB) exceed the 126 MB L2, so no flush is needed.
+value     FP8 attention TFLOPS of the whole job, 4*B*H*S^2*D per step over
+          the CUDA-event time of the step with inputs resident in HBM (max
+          over ranks).  Q/K/V (1 GB) exceed the 126 MB L2, so no flush is needed.
 e2e       the same metric through the public API (vc_attention_b200.attention)
           with a pinned host->device copy of Q/K/V and a device->host copy of
           the output inside every timed step.
@@ -20,8 +21,9 @@ roofline  the fused attention kernel alone, timed with CUDA events on its
           (torch._scaled_mm, 8192^3, E4M3 -> BF16).
 cpu_baseline / --impl reference
           the CPU restatement of the reference backend (oracle/) on the host
-          cores, on a bounded sample (one head, 8 query tiles over all keys,
-          with that head's full preprocessing), scaled to TFLOPS.
+          cores, on a bounded sample (one head: all 256 query tiles over all
+          keys for the baseline leg, 128 per step for --impl reference, with
+          that head's full preprocessing), scaled to TFLOPS.
 """
 from __future__ import annotations
 
@@ -64,14 +66,6 @@ def dist_setup():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=torch.device("cuda", local))
     return world, rank, local
-
-
-def max_over_ranks(x, world):
-    if world == 1:
-        return x
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    return float(t.item())
 
 
 def barrier(world):
@@ -147,7 +141,7 @@ def fp8_peak_tflops(device):
     return 2 * n ** 3 / (best * 1e-3) / 1e12
 
 
-def cpu_reference(threads, heads=1, q_tiles=32):
+def cpu_reference(threads, heads=1, q_tiles=256):
     """Times the CPU restatement of the reference backend on one head: the
     full O(S) preprocessing (Lloyd, Q/K quantisation, V tiles) plus the
     streaming attention of `q_tiles` 128-row query tiles over all S keys."""
@@ -182,8 +176,9 @@ def run_reference(args, world, rank):
         return
     threads = len(os.sched_getaffinity(0))
     times = []
+    q_tiles = 128          # half a head per step: a whole --steps 10 --warmup 3 run stays near a minute
     for i in range(args.warmup + args.steps):
-        r = cpu_reference(threads)
+        r = cpu_reference(threads, q_tiles=q_tiles)
         if i >= args.warmup:
             times.append(r)
     value = statistics.median(x["value"] for x in times)
@@ -191,21 +186,23 @@ def run_reference(args, world, rank):
     cpu["value"] = value
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": flops(1, 1, 32 * 128, S, D) / value / 1e9,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": flops(1, 1, q_tiles * 128, S, D) / value / 1e9,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": dict(CONFIG, global_batch=1, parallelism="cpu"), "cpu_baseline": cpu,
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
 
 
 def run_ours(args, world, rank, local):
-    from vc_attention_b200 import Config, LayoutCache, attention, stages
+    from vc_attention_b200 import Config, LayoutCache, attention, sharding, stages
     from vc_attention_b200.b200_backend import forward, group_values
     from vc_attention_b200.synthetic import make_qkv
 
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     cfg = Config(v_smooth=True, expcast=True)
-    q, k, v = make_qkv("c3", 1000 + rank, device=device)
+    q, k, v = (sharding.shard_heads(x, world, rank) for x in make_qkv("c3", 1000, device=device))
+    h_loc = q.shape[1]
+    torch.cuda.empty_cache()
     scale = D ** -0.5
     out = torch.empty_like(q)
     status = torch.zeros(1, dtype=torch.int32, device=device)
@@ -240,17 +237,17 @@ def run_ours(args, world, rank, local):
     ms = sum(s.elapsed_time(e) for s, e in ev) / args.steps
     if int(status.item()) != 0:
         raise RuntimeError(f"device status flags {int(status.item())}")
-    ms_max = max_over_ranks(ms, world)
-    value = world * flops() / (ms_max * 1e-3) / 1e12
+    ms_max = sharding.max_over_ranks(ms)
+    value = flops() / (ms_max * 1e-3) / 1e12
 
     # dominant kernel alone: the fused attention on prepared operands
     pi, _ = group_values(v, clusters=8, iterations=2)
     q8, qs, k8, ks = stages.quantize_qk(q, k, pi=pi)
     v8, meta = stages.prepare_v(v, pi=pi, active=True)
-    attn_out = torch.empty((H, S, D), dtype=torch.bfloat16, device=device)
+    attn_out = torch.empty((h_loc, S, D), dtype=torch.bfloat16, device=device)
 
     def attn():
-        stages.attention_fp8(q8, qs, k8, ks, v8, meta, heads=H, sq=S, sk=S, dv=D, expcast=True, has_mean=True,
+        stages.attention_fp8(q8, qs, k8, ks, v8, meta, heads=h_loc, sq=S, sk=S, dv=D, expcast=True, has_mean=True,
                              scale=scale, out=attn_out)
 
     for _ in range(3):
@@ -263,8 +260,8 @@ def run_ours(args, world, rank, local):
     e.record()
     e.synchronize()
     attn_ms = s.elapsed_time(e) / reps
-    attn_ms = max_over_ranks(attn_ms, world)
-    achieved = flops() / (attn_ms * 1e-3) / 1e12
+    attn_ms = sharding.max_over_ranks(attn_ms)
+    achieved = flops(h=h_loc) / (attn_ms * 1e-3) / 1e12
     peak = fp8_peak_tflops(device)
     traffic = None
     tfile = ROOT / "profiles" / "attn_kernel_traffic.json"
@@ -288,7 +285,7 @@ def run_ours(args, world, rank, local):
         e.synchronize()
         if i >= args.warmup:
             e2e_ms.append(s.elapsed_time(e))
-    e2e = max_over_ranks(sum(e2e_ms) / len(e2e_ms), world)
+    e2e = sharding.max_over_ranks(sum(e2e_ms) / len(e2e_ms))
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -297,10 +294,12 @@ def run_ours(args, world, rank, local):
         nbytes = q.numel() * q.element_size()
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "e4m3 (bf16 in/out, fp32 accumulate)", "data": "synthetic",
-            "config": dict(CONFIG, global_batch=world, parallelism=f"heads independent, {world} rank(s)"),
-            "e2e": {"value": world * flops() / (e2e * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": e2e,
+            "config": dict(CONFIG, global_batch=1,
+                           parallelism=f"{world} rank(s), {h_loc} heads each (contiguous head ranges), "
+                                       "no collective"),
+            "e2e": {"value": flops() / (e2e * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": e2e,
                     "h2d_bytes_per_step": 3 * nbytes, "d2h_bytes_per_step": nbytes},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": traffic, "kernel": "attn_kernel",

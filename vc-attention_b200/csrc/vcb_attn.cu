@@ -5,25 +5,27 @@
 // GEMM for PV and accumulate, all through HBM scratch) with one CTA per
 // (head, 128-row Q tile) that keeps every intermediate on chip.
 //
-// Roles (512 threads, register budgets rebalanced with setmaxnreg):
+// Roles (640 threads, register budgets rebalanced with setmaxnreg):
 //   warp 0      TMA producer: the Q tile once, then K / V / V-metadata tiles
 //               into a 4-stage ring (no cluster multicast).
 //   warp 1      MMA issuer (one thread): S_j = Q8 K8_j^T into TMEM
 //               (tcgen05.mma kind::f8f6f4, E4M3 x E4M3 -> F32) and
-//               O_j = P_j R_j with P_j and R_j in shared memory.
-//   warps 4-7   softmax, one thread per query row: one TMEM read of the
-//               128 scores, row max, alpha, the ExpCast byte encode (one
-//               packed FMA per pair of scores; the f16-subnormal conversion
-//               rounds to the integer code and clamps it at zero) or
-//               exp + E4M3(p * 256); the row mass; P_j into shared memory.
-//   warps 8-15  correction, two threads per row (64 channels each):
+//               O_j = P_j R_j with P_j in TMEM and R_j in shared memory.
+//   warps 4-11  softmax, two threads per query row (64 scores each; the
+//               halves exchange their partial row maxima): row max, alpha,
+//               the ExpCast byte encode (one packed FMA per pair of scores;
+//               the f16-subnormal conversion rounds to the integer code and
+//               clamps it at zero) or exp + E4M3(p * 256); the row mass;
+//               P_j written back over the thread's own S_j columns.
+//   warps 12-19 correction, two threads per row (64 channels each):
 //               acc = alpha acc + (O_j + M_j mu_j) vscale_j,
 //               den = alpha den + M_j; epilogue acc / den in the output dtype.
 //
 // Latency hiding: S and O are double-buffered in TMEM (S0, S1, O0, O1 use all
-// 512 columns).  The softmax releases S_j as soon as it has read it, so
-// QK_{j+2} runs while the softmax of tile j computes; PV_j only waits for
-// the correction of tile j-2.
+// 512 columns).  P_j lives in S_j's columns, so the MMA issues PV_j and then
+// QK_{j+2} into the same buffer (the tensor pipe keeps issue order); QK_{j+2}
+// runs while the softmax works on tile j+1.  PV_j only waits for the
+// correction of tile j-2.
 //
 // Numerical contract (core.py:307-341): S = (q8 . k8) * qs * ks * scale;
 // ExpCast code = rne(clamp(fma(S - m, 8 log2 e, 119.65), 0, 120)) viewed as
@@ -47,12 +49,11 @@ constexpr uint32_t kTile = 128 * 128;            // one E4M3 tile (16 KB)
 constexpr uint32_t kMetaBytes = 1024;            // vscale[128], mu[128]
 constexpr uint32_t kStageBytes = 2 * kTile + kMetaBytes;
 constexpr uint32_t kOffQ = 0;
-constexpr uint32_t kOffP = kTile;                // P0, P1
-constexpr uint32_t kOffStages = kOffP + 2 * kTile;
+constexpr uint32_t kOffStages = kTile;
 constexpr uint32_t kOffStats = kOffStages + kStages * kStageBytes;   // alpha[4][128], mass[4][2][128]
 constexpr uint32_t kOffXmax = kOffStats + 3 * 4 * 128 * 4;            // partial row max [2][2][128]
 constexpr uint32_t kOffBars = kOffXmax + 2 * 2 * 128 * 4;
-constexpr int kNumBars = 1 + 2 * kStages + 2 * 5 + 2 * 4 + 1 + 8;
+constexpr int kNumBars = 1 + 2 * kStages + 2 * 4 + 2 * 4 + 1 + 8;
 constexpr uint32_t kOffMisc = kOffBars + kNumBars * 8;
 constexpr uint32_t kSmemBytes = kOffMisc + 16;
 constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;
@@ -83,9 +84,8 @@ struct Bars {
     uint64_t* kv_full;     // [kStages]
     uint64_t* kv_empty;    // [kStages]
     uint64_t* s_full;      // [2]  QK_j done
-    uint64_t* s_free;      // [2]  softmax has read S_j
-    uint64_t* p_full;      // [2]  P_j in shared memory
-    uint64_t* o_full;      // [2]  PV_j done (also: P buffer free again)
+    uint64_t* p_full;      // [2]  P_j in TMEM (implies S_j fully read)
+    uint64_t* o_full;      // [2]  PV_j done
     uint64_t* o_free;      // [2]  correction has read O_j
     uint64_t* st_full;     // [4]  alpha / mass of tile j
     uint64_t* st_free;     // [4]
@@ -100,7 +100,6 @@ __device__ __forceinline__ Bars bars_at(uint8_t* smem) {
     r.kv_full = b; b += kStages;
     r.kv_empty = b; b += kStages;
     r.s_full = b; b += 2;
-    r.s_free = b; b += 2;
     r.p_full = b; b += 2;
     r.o_full = b; b += 2;
     r.o_free = b; b += 2;
@@ -171,20 +170,23 @@ __device__ void mma_issuer(const Params& p, uint8_t* smem, const Bars& B, volati
     if (ok && p.T > 1) ok = issue_qk(1);
     for (int j = 0; ok && j < p.T; ++j) {
         const int b = j & 1;
-        if (j + 2 < p.T) {
-            if (!mbar_wait(&B.s_free[b], (j >> 1) & 1, abort) || !issue_qk(j + 2)) break;
-        }
+        // P_j sits in S_j's TMEM columns (each softmax half over its own 64
+        // scores): keys 0-63 at columns 0-15, keys 64-127 at columns 64-79.
         if (!mbar_wait(&B.p_full[b], (j >> 1) & 1, abort)) break;
         if (j >= 2 && !mbar_wait(&B.o_free[b], ((j - 2) >> 1) & 1, abort)) break;
         tc_fence_after();
         const int s = j % kStages;
-        const uint64_t pdesc = smem_desc_k128(smem + kOffP + b * kTile);
         const uint64_t vdesc = smem_desc_k128(smem + kOffStages + s * kStageBytes + kTile);
         const uint32_t d = tmem + kColO + b * 128;
+        const uint32_t pa = tmem + kColS + b * kBN;
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) mma_f8_ss(d, pdesc + 2 * kk, vdesc + 2 * kk, idesc, kk > 0);
+        for (int kk = 0; kk < 4; ++kk)
+            mma_f8_ts(d, pa + (kk >> 1) * 64 + (kk & 1) * 8, vdesc + 2 * kk, idesc, kk > 0);
         mma_commit(&B.o_full[b]);
         mma_commit(&B.kv_empty[s]);
+        // QK_{j+2} overwrites S_j / P_j: the tensor pipe runs in issue order,
+        // so it starts after PV_j has read P_j
+        if (j + 2 < p.T && !issue_qk(j + 2)) break;
     }
     mma_commit(B.drain);
     drain_wait(B.drain, 0);
@@ -207,8 +209,6 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, vola
     float* st_mass = st_alpha + 4 * 128;                       // [4][2][128]
     float* xmax = reinterpret_cast<float*>(smem + kOffXmax);   // [2][2][128]
     const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16) + 64 * hs;
-    uint8_t* prow_base = smem + kOffP + row * 128;
-    const uint32_t swz = (uint32_t)(row & 7);
     const int kstep = p.kq / kBN;
     int kidx = 0, kcnt = 0;
     float m = -INFINITY;
@@ -226,9 +226,6 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, vola
         tmem_ld32_at<0>(ts, r);
         tmem_ld32_at<32>(ts + 32, r);
         tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        mbar_arrive_if(&B.s_free[b], lane == 0);
         const int nvalid = (int)min((int64_t)kBN, p.sk - (int64_t)j * kBN) - 64 * hs;
         if (nvalid < 64) {
 #pragma unroll
@@ -292,17 +289,15 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, vola
         // ms already holds sum(p * 256).
         float M = __fadd_rn(__fadd_rn(ms[0], ms[1]), __fadd_rn(ms[2], ms[3]));
         if (EXPCAST) M = __fmul_rn(M, 256.0f);
-        if (j >= 2 && !mbar_wait(&B.o_full[b], ((j - 2) >> 1) & 1, abort)) break;   // P buffer free
-        uint8_t* prow = prow_base + b * kTile;
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-            *reinterpret_cast<uint4*>(prow + (((uint32_t)(4 * hs + c) ^ swz) << 4)) =
-                make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-        fence_proxy_async_smem();
+        // P_j over this thread's own (already read) S_j columns: 4 codes per
+        // 32-bit column, the A-operand layout of the PV MMA
+        tmem_st16(ts, pk);
         const int slot = j & 3;
         if (j >= 4 && !mbar_wait(&B.st_free[slot], ((j >> 2) - 1) & 1, abort)) break;
         if (hs == 0) st_alpha[slot * 128 + row] = alpha;
         st_mass[(slot * 2 + hs) * 128 + row] = M;
+        tmem_wait_st();
+        tc_fence_before();
         __syncwarp();
         mbar_arrive_if(&B.p_full[b], lane == 0);
         mbar_arrive_if(&B.st_full[slot], lane == 0);
@@ -424,7 +419,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&B.s_full[b], 1);
-            mbar_init(&B.s_free[b], 8);           // 8 softmax warps
             mbar_init(&B.p_full[b], 8);
             mbar_init(&B.o_full[b], 1);
             mbar_init(&B.o_free[b], 8);           // 8 correction warps

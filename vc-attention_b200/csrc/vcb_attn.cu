@@ -51,9 +51,9 @@ constexpr uint32_t kStageBytes = 2 * kTile + kMetaBytes;
 constexpr uint32_t kOffQ = 0;
 constexpr uint32_t kOffStages = kTile;
 constexpr uint32_t kOffStats = kOffStages + kStages * kStageBytes;   // alpha[4][128], mass[4][2][128]
-constexpr uint32_t kOffXmax = kOffStats + 3 * 4 * 128 * 4;            // partial row max [2][2][128]
-constexpr uint32_t kOffBars = kOffXmax + 2 * 2 * 128 * 4;
-constexpr int kNumBars = 1 + 2 * kStages + 2 * 4 + 2 * 4 + 1 + 8;
+constexpr uint32_t kOffXmax = kOffStats + 3 * 4 * 128 * 4;            // {tile + 1, partial max} [2][2][128]
+constexpr uint32_t kOffBars = kOffXmax + 2 * 2 * 128 * 8;
+constexpr int kNumBars = 1 + 2 * kStages + 2 * 4 + 2 * 4 + 1;
 constexpr uint32_t kOffMisc = kOffBars + kNumBars * 8;
 constexpr uint32_t kSmemBytes = kOffMisc + 16;
 constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;
@@ -90,7 +90,6 @@ struct Bars {
     uint64_t* st_full;     // [4]  alpha / mass of tile j
     uint64_t* st_free;     // [4]
     uint64_t* drain;
-    uint64_t* xmax;        // [4 quarters][2]  the two softmax halves of a row exchanged their maxima
 };
 
 __device__ __forceinline__ Bars bars_at(uint8_t* smem) {
@@ -105,8 +104,7 @@ __device__ __forceinline__ Bars bars_at(uint8_t* smem) {
     r.o_free = b; b += 2;
     r.st_full = b; b += 4;
     r.st_free = b; b += 4;
-    r.drain = b; b += 1;
-    r.xmax = b;
+    r.drain = b;
     return r;
 }
 
@@ -123,6 +121,32 @@ __device__ __forceinline__ uint32_t cvt_relu_f16x2(float hi, float lo) {
     uint32_t d;
     asm("cvt.rn.relu.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
     return d;
+}
+
+__device__ __forceinline__ void st_volatile_u64(uint64_t* p, uint64_t v) {
+    asm volatile("st.volatile.shared.u64 [%0], %1;" ::"r"(smem_u32(p)), "l"(v) : "memory");
+}
+
+// Waits until the 64-bit word at p carries `tag` in its upper half and
+// returns its lower half as a float.  Gives up (false) when the CTA aborts or
+// after kWaitLimitNs, setting the abort flag.
+__device__ __forceinline__ bool spin_tagged(const uint64_t* p, uint32_t tag, volatile int* abort, float& val) {
+    const uint32_t a = smem_u32(p);
+    uint64_t v;
+    asm volatile("ld.volatile.shared.u64 %0, [%1];" : "=l"(v) : "r"(a) : "memory");
+    if ((uint32_t)(v >> 32) != tag) {
+        const uint64_t t0 = globaltimer();
+        for (uint32_t i = 1;; ++i) {
+            asm volatile("ld.volatile.shared.u64 %0, [%1];" : "=l"(v) : "r"(a) : "memory");
+            if ((uint32_t)(v >> 32) == tag) break;
+            if ((i & 31u) == 0) {
+                if (*abort) return false;
+                if (globaltimer() - t0 > kWaitLimitNs) { *abort = 1; return false; }
+            }
+        }
+    }
+    val = __uint_as_float((uint32_t)v);
+    return true;
 }
 
 __device__ void producer(const Params& p, uint8_t* smem, const Bars& B, volatile int* abort, int qtile,
@@ -207,7 +231,7 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, vola
     const float* ksp = p.k_scale + (int64_t)head * p.nkb;
     float* st_alpha = reinterpret_cast<float*>(smem + kOffStats);
     float* st_mass = st_alpha + 4 * 128;                       // [4][2][128]
-    float* xmax = reinterpret_cast<float*>(smem + kOffXmax);   // [2][2][128]
+    uint64_t* xmax = reinterpret_cast<uint64_t*>(smem + kOffXmax);   // [2][2][128]
     const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16) + 64 * hs;
     const int kstep = p.kq / kBN;
     int kidx = 0, kcnt = 0;
@@ -241,11 +265,13 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, vola
             for (int k = 0; k < 4; ++k)
                 mx[k] = fmax3(mx[k], __uint_as_float(r[8 * t + 2 * k]), __uint_as_float(r[8 * t + 2 * k + 1]));
         const float pmax = fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]);
-        xmax[(b * 2 + hs) * 128 + row] = pmax;
-        __syncwarp();
-        mbar_arrive_if(&B.xmax[quarter * 2 + b], lane == 0);
-        if (!mbar_wait(&B.xmax[quarter * 2 + b], (j >> 1) & 1, abort)) break;
-        const float rmax = fmaxf(pmax, xmax[(b * 2 + (hs ^ 1)) * 128 + row]);
+        // The two halves of a row swap partial maxima through one 64-bit
+        // word each: {tile + 1, max}, written and read whole, so the tag
+        // says when the value is there (bounded spin).
+        st_volatile_u64(&xmax[(b * 2 + hs) * 128 + row], ((uint64_t)(j + 1) << 32) | __float_as_uint(pmax));
+        float omax;
+        if (!spin_tagged(&xmax[(b * 2 + (hs ^ 1)) * 128 + row], (uint32_t)(j + 1), abort, omax)) break;
+        const float rmax = fmaxf(pmax, omax);
         const float c = __fmul_rn(__fmul_rn(qs_scale, ks), p.scale);
         const float m_new = fmaxf(m, __fmul_rn(rmax, c));
         const float alpha = expf(m - m_new);
@@ -334,6 +360,10 @@ __device__ void correction_role(const Params& p, uint8_t* smem, const Bars& B, v
         const bool rescale = __any_sync(0xffffffffu, alpha != 1.0f);
         const float2 aa = make_float2(alpha, alpha), MM = make_float2(M, M);
         const uint32_t to = trow + kColO + b * 128 + c0;
+        if (rescale) {      // warp-uniform; alpha == 1 leaves acc unchanged
+#pragma unroll
+            for (int i = 0; i < 32; ++i) acc[i] = fmul2(acc[i], aa);
+        }
 #pragma unroll
         for (int ch = 0; ch < 2; ++ch) {
             uint32_t o[32];
@@ -356,7 +386,6 @@ __device__ void correction_role(const Params& p, uint8_t* smem, const Bars& B, v
                     float2 x = make_float2(__uint_as_float(o[k]), __uint_as_float(o[k + 1]));
                     const float2 v2 = h ? make_float2(vs.z, vs.w) : make_float2(vs.x, vs.y);
                     if (HAS_MEAN) x = ffma2(MM, h ? make_float2(mu.z, mu.w) : make_float2(mu.x, mu.y), x);
-                    if (rescale) acc[i] = fmul2(acc[i], aa);      // warp-uniform
                     acc[i] = ffma2(x, v2, acc[i]);
                 }
             }
@@ -411,6 +440,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int qtile = blockIdx.x, head = blockIdx.y;
 
+    for (int i = threadIdx.x; i < 2 * 2 * 128; i += kThreads)
+        reinterpret_cast<uint64_t*>(smem + kOffXmax)[i] = 0;
     if (threadIdx.x == 0) {
         mbar_init(B.q_full, 1);
         for (int s = 0; s < kStages; ++s) {
@@ -428,7 +459,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
             mbar_init(&B.st_free[s], 8);
         }
         mbar_init(B.drain, 1);
-        for (int i = 0; i < 8; ++i) mbar_init(&B.xmax[i], 2);   // the two softmax warps of a quarter
         *abort = 0;
         fence_barrier_init();
     }

@@ -152,18 +152,22 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parit
 
 // A wait that gives up: after kWaitLimitNs, or as soon as another role has
 // raised *abort, it returns false (and raises *abort itself on timeout).  No
-// wait in these kernels can spin forever.
+// wait in these kernels can spin forever.  The hot waits poll with the plain
+// try_wait (its wake-up is quicker than the suspend-hint form) and look at the
+// abort flag and the clock every 16 polls.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;   // 2 s, far above any real wait
-constexpr uint32_t kSuspendHintNs = 1000000u;      // re-check abort / deadline every ~1 ms
+constexpr uint32_t kSuspendHintNs = 1000000u;      // drain waits: re-check the deadline every ~1 ms
 
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
     const uint32_t a = smem_u32(bar);
-    if (mbar_try_wait_sleep(a, parity, kSuspendHintNs)) return true;
+    if (mbar_try_wait(a, parity)) return true;
     const uint64_t t0 = globaltimer();
-    for (;;) {
-        if (mbar_try_wait_sleep(a, parity, kSuspendHintNs)) return true;
-        if (*abort) return false;
-        if (globaltimer() - t0 > kWaitLimitNs) { *abort = 1; return false; }
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait(a, parity)) return true;
+        if ((i & 15u) == 0) {
+            if (*abort) return false;
+            if (globaltimer() - t0 > kWaitLimitNs) { *abort = 1; return false; }
+        }
     }
 }
 

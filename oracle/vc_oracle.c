@@ -20,9 +20,11 @@
  *   V block mean     : per (tile, channel) tokens are added in tile order.
  *   Lloyd distances  : ||x||^2, ||c||^2 and x.c are fmaf chains over channels
  *                      0..D-1; distance = (xx + cc) - 2*xc, first minimum wins.
- *   Lloyd sums       : tokens are split into chunks of VCO_LLOYD_CHUNK; inside
- *                      a chunk each cluster sums its tokens in token order;
- *                      chunks are added in order; centre = sum / count.
+ *   Lloyd sums       : tokens are split into chunks of VCO_LLOYD_CHUNK and
+ *                      each chunk into sub-chunks of VCO_LLOYD_SUB; inside a
+ *                      sub-chunk each cluster sums its tokens in token order;
+ *                      a chunk adds its sub-chunk sums in order (from 0), the
+ *                      total adds chunk sums in order; centre = sum / count.
  *
  * Build: see oracle/Makefile (gcc -O2 -ffp-contract=off, no fast-math).
  */
@@ -34,6 +36,7 @@
 #define VCO_KSUM_CHUNK 256
 #define VCO_KSUM_LANES 16
 #define VCO_LLOYD_CHUNK 256
+#define VCO_LLOYD_SUB 32
 
 static inline uint32_t f2u(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
 static inline float u2f(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
@@ -43,6 +46,7 @@ int vco_constants(int which) {
         case 0: return VCO_KSUM_CHUNK;
         case 1: return VCO_KSUM_LANES;
         case 2: return VCO_LLOYD_CHUNK;
+        case 3: return VCO_LLOYD_SUB;
         default: return -1;
     }
 }
@@ -223,6 +227,7 @@ int vco_group_values(const float* v, int64_t heads, int64_t S, int D, int cluste
     float* cen = (float*)malloc(sizeof(float) * count * D);
     float* sums = (float*)malloc(sizeof(float) * count * D);
     float* part = (float*)malloc(sizeof(float) * count * D);
+    float* sub = (float*)malloc(sizeof(float) * count * D);
     int64_t* counts = (int64_t*)malloc(sizeof(int64_t) * count);
     float* cnorm = (float*)malloc(sizeof(float) * count);
     vco_linspace_indices(S, count, idx);
@@ -250,10 +255,15 @@ int vco_group_values(const float* v, int64_t heads, int64_t S, int D, int cluste
                     lab[t] = (uint8_t)best;
                 }
                 memset(part, 0, sizeof(float) * count * D);
-                for (int64_t t = base; t < end; ++t) {
-                    int c = lab[t];
-                    counts[c] += 1;
-                    for (int d = 0; d < D; ++d) part[c * D + d] += vh[t * D + d];
+                for (int64_t sb = base; sb < end; sb += VCO_LLOYD_SUB) {
+                    int64_t se = sb + VCO_LLOYD_SUB < end ? sb + VCO_LLOYD_SUB : end;
+                    memset(sub, 0, sizeof(float) * count * D);
+                    for (int64_t t = sb; t < se; ++t) {
+                        int c = lab[t];
+                        counts[c] += 1;
+                        for (int d = 0; d < D; ++d) sub[c * D + d] += vh[t * D + d];
+                    }
+                    for (int i = 0; i < count * D; ++i) part[i] += sub[i];
                 }
                 for (int i = 0; i < count * D; ++i) sums[i] += part[i];
             }
@@ -269,7 +279,7 @@ int vco_group_values(const float* v, int64_t heads, int64_t S, int D, int cluste
         for (int c = 0; c < count; ++c) start[c + 1] += start[c];
         for (int64_t t = 0; t < S; ++t) pi[h * S + start[lab[t]]++] = (int32_t)t;
     }
-    free(cen); free(sums); free(part); free(counts); free(cnorm);
+    free(cen); free(sums); free(part); free(sub); free(counts); free(cnorm);
     return count;
 }
 

@@ -6,8 +6,10 @@
 // Fixed orders, mirrored by the CPU checker:
 //   distances  ||x||^2, ||c||^2 and x.c are fmaf chains over channels
 //              0..D-1; distance = (xx + cc) - 2*xc; the first minimum wins.
-//   sums       chunks of kChunk tokens; inside a chunk each cluster adds its
-//              tokens in token order; chunks are added in order.
+//   sums       chunks of kChunk tokens, each split into sub-chunks of kSub
+//              tokens; inside a sub-chunk each cluster adds its tokens in
+//              token order; a chunk adds its sub-chunk sums in order (from
+//              0); chunks are added in order.
 //   permutation  a counting sort: cluster-major, token order inside a
 //              cluster, i.e. argsort(labels, stable=True).
 #include "vcb_internal.h"
@@ -15,6 +17,7 @@
 namespace vcb {
 
 constexpr int kChunk = 256;
+constexpr int kSub = 32;
 constexpr int kMaxClusters = 32;
 
 struct ClusterArgs {
@@ -32,6 +35,10 @@ struct ClusterArgs {
 };
 
 struct InitIdx { long long idx[kMaxClusters]; };
+
+__device__ __forceinline__ float to_float(float x) { return x; }
+__device__ __forceinline__ float to_float(__half x) { return __half2float(x); }
+__device__ __forceinline__ float to_float(__nv_bfloat16 x) { return __bfloat162float(x); }
 
 template <typename T>
 __global__ void cluster_init_kernel(ClusterArgs a, const float* __restrict__ centers_in, InitIdx init) {
@@ -143,21 +150,189 @@ __global__ void __launch_bounds__(256) cluster_assign_kernel(ClusterArgs a) {
         order[seg[lj] + before + rank_in_warp] = (uint16_t)tid;
     }
     __syncthreads();
-    // Per-cluster partial sums: each cluster's tokens in token order, the
-    // fixed order the CPU checker uses.  Threads 0..127 own clusters below
-    // count/2, threads 128..255 the rest; channel d = tid % 128.
+    // Per-cluster partial sums in the fixed order the CPU checker uses: a
+    // cluster's tokens in token order inside each kSub sub-chunk, sub-chunk
+    // sums added in order.  Threads 0..127 own clusters below count/2,
+    // threads 128..255 the rest; channel d = tid % 128.
     const int d = tid & 127;
     const int c_lo = tid < 128 ? 0 : count / 2, c_hi = tid < 128 ? count / 2 : count;
     float* ps = a.psum + ((int64_t)h * a.nchunk + chunk) * count * 128;
     if (d < D) {
         for (int c = c_lo; c < c_hi; ++c) {
-            float sum = 0.0f;
+            float part = 0.0f, sub = 0.0f;
+            int cur = -1;
             const int p1 = seg[c + 1];
-            for (int pos = seg[c]; pos < p1; ++pos) sum += Elem<T>::load(vh + (base + order[pos]) * D + d);
-            ps[c * 128 + d] = sum;
+            for (int pos = seg[c]; pos < p1; ++pos) {
+                const int tok = order[pos];
+                if (tok / kSub != cur) {   // a new sub-chunk: close the previous one
+                    part += sub;
+                    sub = 0.0f;
+                    cur = tok / kSub;
+                }
+                sub += Elem<T>::load(vh + (base + tok) * D + d);
+            }
+            ps[c * 128 + d] = part + sub;
         }
     }
     if (tid < count) a.pcnt[((int64_t)h * a.nchunk + chunk) * count + tid] = seg[tid + 1] - seg[tid];
+}
+
+// D == 128: the chunk's rows are staged in shared memory once (coalesced
+// 16-byte loads, 16-byte chunks XOR-swizzled by row so that a warp reading
+// one chunk of 32 rows hits every bank group), then
+//   distances  thread t = token t, channels streamed in order from shared
+//              memory (same fmaf chains as above);
+//   sums       warp w = sub-chunk w (tokens 32w..32w+31), lane = 4 channels,
+//              the token loop in order with a warp-uniform switch on the
+//              label; sub-chunk sums added in order by thread (cluster, d).
+template <typename T>
+__global__ void __launch_bounds__(256, 2) cluster_assign128_kernel(ClusterArgs a) {
+    constexpr int RB = 128 * (int)sizeof(T);        // bytes per staged row
+    constexpr int NCH = RB / 16;                    // 16-byte chunks per row
+    constexpr int E = 16 / (int)sizeof(T);          // elements per chunk
+    extern __shared__ __align__(16) uint8_t dsm[];
+    uint8_t* xs = dsm;                                               // [256][RB], swizzled
+    float* subs = reinterpret_cast<float*>(dsm + kChunk * RB);        // [8 warps][8 clusters][128]
+    __shared__ __align__(16) float cen[kMaxClusters * 128];
+    __shared__ float cnorm[kMaxClusters];
+    __shared__ uint8_t lab[kChunk];
+    __shared__ int cnt[kMaxClusters];
+    const int64_t h = blockIdx.y;
+    const int chunk = blockIdx.x;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int count = a.count;
+    const int64_t base = (int64_t)chunk * kChunk;
+    const int nvalid = (int)min((int64_t)kChunk, a.S - base);
+    for (int i = tid; i < kMaxClusters * 128; i += 256) {
+        const int c = i / 128;
+        cen[i] = c < count ? a.centers[(h * count) * 128 + i] : 0.0f;
+    }
+    if (tid < kMaxClusters) cnt[tid] = 0;
+    const uint4* src = reinterpret_cast<const uint4*>(static_cast<const T*>(a.v) + (h * a.S + base) * 128);
+    {   // every load of the chunk in flight before the first store
+        constexpr int kPer = kChunk * NCH / 256;
+        constexpr int kRound = kPer < 16 ? kPer : 16;
+#pragma unroll
+        for (int u0 = 0; u0 < kPer; u0 += kRound) {
+            uint4 buf[kRound];
+#pragma unroll
+            for (int u = 0; u < kRound; ++u) {
+                const int g = tid + 256 * (u0 + u);
+                if (g / NCH < nvalid) buf[u] = __ldg(src + g);
+            }
+#pragma unroll
+            for (int u = 0; u < kRound; ++u) {
+                const int g = tid + 256 * (u0 + u), r = g / NCH, k = g % NCH;
+                if (r < nvalid) *reinterpret_cast<uint4*>(xs + r * RB + ((k ^ (r & (NCH - 1))) << 4)) = buf[u];
+            }
+        }
+    }
+    __syncthreads();
+    if (tid < count) {
+        float acc = 0.0f;
+        for (int d = 0; d < 128; ++d) acc = fmaf(cen[tid * 128 + d], cen[tid * 128 + d], acc);
+        cnorm[tid] = acc;
+    }
+    __syncthreads();
+
+    if (tid < nvalid) {
+        const uint8_t* xr = xs + tid * RB;
+        const int sw = tid & (NCH - 1);
+        float xx = 0.0f, bestd = 0.0f;
+        int best = 0;
+        for (int c0 = 0; c0 < count; c0 += 8) {
+            float acc[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+#pragma unroll 2
+            for (int k = 0; k < NCH; ++k) {
+                const uint4 raw = *reinterpret_cast<const uint4*>(xr + ((k ^ sw) << 4));
+                float x[E];
+                if constexpr (sizeof(T) == 4) {
+                    x[0] = __uint_as_float(raw.x); x[1] = __uint_as_float(raw.y);
+                    x[2] = __uint_as_float(raw.z); x[3] = __uint_as_float(raw.w);
+                } else {
+                    const T* hv = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) x[e] = to_float(hv[e]);
+                }
+#pragma unroll
+                for (int e0 = 0; e0 < E; e0 += 4) {
+                    const int d = k * E + e0;
+                    if (c0 == 0) {
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) xx = fmaf(x[e0 + e], x[e0 + e], xx);
+                    }
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const float4 cv = *reinterpret_cast<const float4*>(&cen[(c0 + i) * 128 + d]);
+                        acc[i] = fmaf(x[e0], cv.x, acc[i]);
+                        acc[i] = fmaf(x[e0 + 1], cv.y, acc[i]);
+                        acc[i] = fmaf(x[e0 + 2], cv.z, acc[i]);
+                        acc[i] = fmaf(x[e0 + 3], cv.w, acc[i]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int c = c0 + i;
+                if (c < count) {
+                    const float dist = __fsub_rn(__fadd_rn(xx, cnorm[c]), __fmul_rn(2.0f, acc[i]));
+                    if (c == 0 || dist < bestd) { bestd = dist; best = c; }
+                }
+            }
+        }
+        lab[tid] = (uint8_t)best;
+        a.labels[h * a.S + base + tid] = (uint8_t)best;
+        atomicAdd(&cnt[best], 1);
+    }
+    __syncthreads();
+
+    float* ps = a.psum + ((int64_t)h * a.nchunk + chunk) * count * 128;
+    const int t0 = warp * kSub, t1 = min(t0 + kSub, nvalid);
+    for (int cg = 0; cg < count; cg += 8) {
+        float s[8][4];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) s[i][e] = 0.0f;
+        for (int t = t0; t < t1; ++t) {
+            const int c = lab[t] - cg;
+            if (c < 0 || c >= 8) continue;              // warp-uniform
+            float x[4];
+            const uint8_t* xr = xs + t * RB;
+            if constexpr (sizeof(T) == 4) {
+                const float4 v = *reinterpret_cast<const float4*>(xr + ((lane ^ (t & (NCH - 1))) << 4));
+                x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+            } else {
+                const uint2 raw = *reinterpret_cast<const uint2*>(xr + (((lane >> 1) ^ (t & (NCH - 1))) << 4) +
+                                                                  (lane & 1) * 8);
+                const T* hv = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) x[e] = to_float(hv[e]);
+            }
+            switch (c) {
+#define VCB_ADD4(I) case I: s[I][0] += x[0]; s[I][1] += x[1]; s[I][2] += x[2]; s[I][3] += x[3]; break;
+                VCB_ADD4(0) VCB_ADD4(1) VCB_ADD4(2) VCB_ADD4(3) VCB_ADD4(4) VCB_ADD4(5) VCB_ADD4(6) VCB_ADD4(7)
+#undef VCB_ADD4
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            *reinterpret_cast<float4*>(&subs[(warp * 8 + i) * 128 + 4 * lane]) =
+                make_float4(s[i][0], s[i][1], s[i][2], s[i][3]);
+        __syncthreads();
+        for (int idx = tid; idx < 8 * 128; idx += 256) {
+            const int i = idx >> 7, d = idx & 127;
+            if (cg + i >= count) continue;
+            float part = 0.0f;
+#pragma unroll
+            for (int w = 0; w < 8; ++w) part += subs[(w * 8 + i) * 128 + d];
+            ps[(cg + i) * 128 + d] = part;
+        }
+        __syncthreads();
+    }
+    if (tid < count) a.pcnt[((int64_t)h * a.nchunk + chunk) * count + tid] = cnt[tid];
 }
 
 // One CTA per (head, cluster), thread d per channel; chunks added in order
@@ -242,8 +417,15 @@ int run(const vcb_group_args* p, cudaStream_t st) {
     linspace_indices(p->s, count, init.idx);
     cluster_init_kernel<T><<<(unsigned)p->heads, 256, 0, st>>>(a, p->centers_in, init);
     VCB_CUDA(cudaGetLastError());
+    const size_t fast_smem = (size_t)kChunk * 128 * sizeof(T) + 8 * 8 * 128 * sizeof(float);
+    if (p->d == 128)
+        VCB_CUDA(cudaFuncSetAttribute(cluster_assign128_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)fast_smem));
     for (int it = 0; it < p->iterations; ++it) {
-        cluster_assign_kernel<T><<<dim3(nchunk, (unsigned)p->heads), 256, 0, st>>>(a);
+        if (p->d == 128)
+            cluster_assign128_kernel<T><<<dim3(nchunk, (unsigned)p->heads), 256, fast_smem, st>>>(a);
+        else
+            cluster_assign_kernel<T><<<dim3(nchunk, (unsigned)p->heads), 256, 0, st>>>(a);
         VCB_CUDA(cudaGetLastError());
         cluster_update_kernel<<<dim3((unsigned)p->heads, (unsigned)count), 128, 0, st>>>(a);
         VCB_CUDA(cudaGetLastError());

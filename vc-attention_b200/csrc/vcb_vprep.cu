@@ -15,6 +15,10 @@ namespace vcb {
 
 constexpr int kTile = 128;
 
+__device__ __forceinline__ float to_float(float x) { return x; }
+__device__ __forceinline__ float to_float(__half x) { return __half2float(x); }
+__device__ __forceinline__ float to_float(__nv_bfloat16 x) { return __bfloat162float(x); }
+
 template <typename T>
 __global__ void __launch_bounds__(128) vprep_kernel(const T* __restrict__ v, int64_t S, int dv,
                                                     const int32_t* __restrict__ pi, int active,
@@ -27,11 +31,44 @@ __global__ void __launch_bounds__(128) vprep_kernel(const T* __restrict__ v, int
     const int cnt = (int)min((int64_t)kTile, S - s0);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     bool ok = true;
+    __shared__ int64_t toks[kTile];
+    if ((int)threadIdx.x < cnt) toks[threadIdx.x] = pi ? (int64_t)pi[h * S + s0 + threadIdx.x] : s0 + threadIdx.x;
+    __syncthreads();
+    if (dv == 128 && (reinterpret_cast<uintptr_t>(v) & 15) == 0) {
+        // Rows of 16-byte pieces, every load of the tile in flight at once.
+        constexpr int E = 16 / (int)sizeof(T);        // elements per piece
+        constexpr int NP = 128 / E;                   // pieces per row
+        constexpr int kPer = kTile * NP / 128;        // pieces per thread
+        constexpr int kRound = kPer < 16 ? kPer : 16;
+#pragma unroll
+        for (int u0 = 0; u0 < kPer; u0 += kRound) {
+            uint4 buf[kRound];
+#pragma unroll
+            for (int u = 0; u < kRound; ++u) {
+                const int g = threadIdx.x + 128 * (u0 + u), j = g / NP, k = g % NP;
+                buf[u] = j < cnt ? __ldg(reinterpret_cast<const uint4*>(v + (h * S + toks[j]) * 128) + k)
+                                 : make_uint4(0u, 0u, 0u, 0u);
+            }
+#pragma unroll
+            for (int u = 0; u < kRound; ++u) {
+                const int g = threadIdx.x + 128 * (u0 + u), j = g / NP, k = g % NP;
+                float e[E];
+                const T* hv = reinterpret_cast<const T*>(&buf[u]);
+#pragma unroll
+                for (int i = 0; i < E; ++i) {
+                    e[i] = to_float(hv[i]);
+                    ok &= finite_f(e[i]);
+                }
+                float4* dst = reinterpret_cast<float4*>(tile + j * 128 + k * E);
+#pragma unroll
+                for (int i = 0; i < E / 4; ++i) dst[i] = make_float4(e[4 * i], e[4 * i + 1], e[4 * i + 2], e[4 * i + 3]);
+            }
+        }
+    } else
     for (int j = warp; j < kTile; j += 4) {
         float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
         if (j < cnt) {
-            const int64_t tok = pi ? (int64_t)pi[h * S + s0 + j] : s0 + j;
-            const T* row = v + (h * S + tok) * dv;
+            const T* row = v + (h * S + toks[j]) * dv;
             float e[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {

@@ -132,36 +132,40 @@ __device__ __forceinline__ bool transform_row(const RowArgs& a, int64_t h, int64
 // butterflies with stride 1..32 stay inside a half; the stride-64 stage
 // exchanges halves with one shuffle per element and still computes
 // (left + right, left - right) on the same operands.
-template <typename T>
+// FIX: D == 128 with the 128-point Hadamard, every bound known at compile time.
+template <typename T, bool FIX>
 __device__ __forceinline__ bool transform_half(const RowArgs& a, int64_t h, int64_t r, bool valid, int half,
-                                               const float* smean, float (&x)[64]) {
+                                               const float* smean, float (&x)[64], int64_t tok_hint = -1) {
     bool ok = true;
     const int c0 = 64 * half;
+    const int D = FIX ? 128 : a.D;
+    const int width = FIX ? 128 : a.width;
+    const bool hadamard = FIX ? true : a.hadamard != 0;
     if (valid) {
-        const int64_t tok = a.pi ? (int64_t)a.pi[h * a.S + r] : r;
-        const T* src = static_cast<const T*>(a.x) + (h * a.S + tok) * a.D;
-        if (a.D == 128) {
+        const int64_t tok = tok_hint >= 0 ? tok_hint : a.pi ? (int64_t)a.pi[h * a.S + r] : r;
+        const T* src = static_cast<const T*>(a.x) + (h * a.S + tok) * D;
+        if (D == 128) {
 #pragma unroll
             for (int i = 0; i < 8; ++i) load8(src + c0 + 8 * i, x + 8 * i);
         } else {
 #pragma unroll
-            for (int c = 0; c < 64; ++c) x[c] = c0 + c < a.D ? Elem<T>::load(src + c0 + c) : 0.0f;
+            for (int c = 0; c < 64; ++c) x[c] = c0 + c < D ? Elem<T>::load(src + c0 + c) : 0.0f;
         }
 #pragma unroll
         for (int c = 0; c < 64; ++c) ok &= finite_f(x[c]);
         if (smean) {
 #pragma unroll
             for (int c = 0; c < 64; ++c)
-                if (c0 + c < a.D) x[c] = x[c] - smean[c0 + c];
+                if (c0 + c < D) x[c] = x[c] - smean[c0 + c];
         }
     } else {
 #pragma unroll
         for (int c = 0; c < 64; ++c) x[c] = 0.0f;
     }
-    if (a.hadamard) {
+    if (hadamard) {
 #pragma unroll
         for (int s = 1; s < 64; s <<= 1) {
-            if (s < a.width) {
+            if (s < width) {
 #pragma unroll
                 for (int base = 0; base < 64; base += 2 * s) {
 #pragma unroll
@@ -173,16 +177,17 @@ __device__ __forceinline__ bool transform_half(const RowArgs& a, int64_t h, int6
                 }
             }
         }
-        if (a.width > 64) {
+        if (width > 64) {
 #pragma unroll
             for (int c = 0; c < 64; ++c) {
                 const float other = __shfl_xor_sync(0xffffffffu, x[c], 16);
                 x[c] = half == 0 ? x[c] + other : other - x[c];
             }
         }
+        const float norm = FIX ? 0.08838834764831845f : a.norm;     // fp32(128^-0.5)
 #pragma unroll
         for (int c = 0; c < 64; ++c)
-            if (c0 + c < a.width) x[c] = x[c] * a.norm;
+            if (c0 + c < width) x[c] = x[c] * norm;
     }
     return ok;
 }
@@ -211,9 +216,10 @@ __device__ __forceinline__ void encode_half(const float (&x)[64], int c0, int W,
 // One CTA per quantisation block, two threads per row, 256 rows per pass.
 // Blocks of at most 256 rows keep the transformed halves in registers from
 // the amax to the encode; larger blocks re-read and re-transform in pass 2.
-template <typename T>
+template <typename T, bool FIX>
 __global__ void __launch_bounds__(512) qk_quant_kernel(RowArgs a) {
     __shared__ float smean[128];
+    __shared__ int32_t stok[256];
     __shared__ float red[16];
     __shared__ float sdiv[3];
     const int64_t h = blockIdx.y;
@@ -221,14 +227,17 @@ __global__ void __launch_bounds__(512) qk_quant_kernel(RowArgs a) {
     const int nthr = blockDim.x;
     if (a.mean)
         for (int c = threadIdx.x; c < 128; c += nthr) smean[c] = a.mean[h * 128 + c];
+    const int64_t r0 = (int64_t)b * a.block;
+    const bool single = a.block <= nthr / 2;
+    if (single && a.pi)      // the block's permuted rows, read once and early
+        for (int i = threadIdx.x; i < a.block; i += nthr)
+            stok[i] = r0 + i < a.S ? a.pi[h * a.S + r0 + i] : 0;
     __syncthreads();
     const float* sm = a.mean ? smean : nullptr;
-    const int W = a.hadamard ? a.width : a.D;
+    const int W = FIX ? 128 : a.hadamard ? a.width : a.D;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int half = lane >> 4;
     const int rows_per_pass = nthr / 2;
-    const int64_t r0 = (int64_t)b * a.block;
-    const bool single = a.block <= rows_per_pass;
     float x[64];
     float amax = 0.0f;
     bool ok = true;
@@ -236,7 +245,8 @@ __global__ void __launch_bounds__(512) qk_quant_kernel(RowArgs a) {
         const int rl = base + warp * 16 + (lane & 15);
         const int64_t r = r0 + rl;
         const bool valid = rl < a.block && r < a.S;
-        ok &= transform_half<T>(a, h, r, valid, half, sm, x);
+        const int64_t tok = single ? (a.pi ? (valid ? (int64_t)stok[rl] : 0) : r) : -1;
+        ok &= transform_half<T, FIX>(a, h, r, valid, half, sm, x, tok);
 #pragma unroll
         for (int c = 0; c < 64; ++c)
             if (64 * half + c < W) amax = fmaxf(amax, fabsf(x[c]));
@@ -262,7 +272,7 @@ __global__ void __launch_bounds__(512) qk_quant_kernel(RowArgs a) {
         const int rl = base + warp * 16 + (lane & 15);
         const int64_t r = r0 + rl;
         const bool valid = rl < a.block && r < a.S;
-        if (!single) transform_half<T>(a, h, r, valid, half, sm, x);   // warp-uniform
+        if (!single) transform_half<T, FIX>(a, h, r, valid, half, sm, x);   // warp-uniform
         if (rl >= a.block || r >= a.S_pad) continue;
         uint4* dst = reinterpret_cast<uint4*>(a.payload + (h * a.S_pad + r) * 128 + 64 * half);
         if (!valid) {
@@ -319,7 +329,10 @@ int launch_rows(const RowArgs& a, int64_t heads, bool quantise, cudaStream_t st)
         const unsigned grid = (unsigned)(a.S_pad / a.block);
         const int rows = a.block < 256 ? a.block : 256;
         const int nthr = (rows + 15) / 16 * 32;      // two threads per row, whole warps
-        qk_quant_kernel<T><<<dim3(grid, (unsigned)heads), nthr, 0, st>>>(a);
+        if (a.D == 128 && a.hadamard)
+            qk_quant_kernel<T, true><<<dim3(grid, (unsigned)heads), nthr, 0, st>>>(a);
+        else
+            qk_quant_kernel<T, false><<<dim3(grid, (unsigned)heads), nthr, 0, st>>>(a);
     } else {
         qk_transform_kernel<T><<<dim3((unsigned)((a.S + 127) / 128), (unsigned)heads), 128, 0, st>>>(a);
     }

@@ -6,8 +6,9 @@
 // (head, 128-row Q tile) that keeps every intermediate on chip.
 //
 // Roles (640 threads, register budgets rebalanced with setmaxnreg):
-//   warp 0      TMA producer: the Q tile once, then K / V / V-metadata tiles
-//               into a 4-stage ring (no cluster multicast).
+//   warp 0      TMA producer: the Q tile once, then K / V tiles into a 4-stage
+//               ring (no cluster multicast).
+//   warp 2      the per-tile V scales and means into a 16-slot ring.
 //   warp 1      MMA issuer (one thread): S_j = Q8 K8_j^T into TMEM
 //               (tcgen05.mma kind::f8f6f4, E4M3 x E4M3 -> F32) and
 //               O_j = P_j R_j with P_j in TMEM and R_j in shared memory.
@@ -44,16 +45,18 @@ namespace {
 constexpr int kBM = 128;
 constexpr int kBN = 128;
 constexpr int kStages = 4;
+constexpr int kMetaSlots = 16;                   // per-tile vscale / mu ring
 constexpr int kThreads = 640;                    // 20 warps: 4 producer/MMA, 8 softmax, 8 correction
 constexpr uint32_t kTile = 128 * 128;            // one E4M3 tile (16 KB)
 constexpr uint32_t kMetaBytes = 1024;            // vscale[128], mu[128]
-constexpr uint32_t kStageBytes = 2 * kTile + kMetaBytes;
+constexpr uint32_t kStageBytes = 2 * kTile;      // K tile, V tile
 constexpr uint32_t kOffQ = 0;
 constexpr uint32_t kOffStages = kTile;
-constexpr uint32_t kOffStats = kOffStages + kStages * kStageBytes;   // alpha[4][128], mass[4][2][128]
+constexpr uint32_t kOffMeta = kOffStages + kStages * kStageBytes;    // vscale[128], mu[128] per slot
+constexpr uint32_t kOffStats = kOffMeta + kMetaSlots * kMetaBytes;   // alpha[4][128], mass[4][2][128]
 constexpr uint32_t kOffXmax = kOffStats + 3 * 4 * 128 * 4;            // {tile + 1, partial max} [2][2][128]
 constexpr uint32_t kOffBars = kOffXmax + 2 * 2 * 128 * 8;
-constexpr int kNumBars = 1 + 2 * kStages + 2 * 4 + 2 * 4 + 1;
+constexpr int kNumBars = 1 + 2 * kStages + 2 * kMetaSlots + 2 * 4 + 2 * 4 + 1;
 constexpr uint32_t kOffMisc = kOffBars + kNumBars * 8;
 constexpr uint32_t kSmemBytes = kOffMisc + 16;
 constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;
@@ -82,7 +85,9 @@ struct Params {
 struct Bars {
     uint64_t* q_full;
     uint64_t* kv_full;     // [kStages]
-    uint64_t* kv_empty;    // [kStages]
+    uint64_t* kv_empty;    // [kStages]     PV of the stage's tile committed
+    uint64_t* meta_full;   // [kMetaSlots]
+    uint64_t* meta_empty;  // [kMetaSlots]  the 8 correction warps have read the slot
     uint64_t* s_full;      // [2]  QK_j done
     uint64_t* p_full;      // [2]  P_j in TMEM (implies S_j fully read)
     uint64_t* o_full;      // [2]  PV_j done
@@ -98,6 +103,8 @@ __device__ __forceinline__ Bars bars_at(uint8_t* smem) {
     r.q_full = b; b += 1;
     r.kv_full = b; b += kStages;
     r.kv_empty = b; b += kStages;
+    r.meta_full = b; b += kMetaSlots;
+    r.meta_empty = b; b += kMetaSlots;
     r.s_full = b; b += 2;
     r.p_full = b; b += 2;
     r.o_full = b; b += 2;
@@ -156,16 +163,14 @@ __device__ void producer(const Params& p, uint8_t* smem, const Bars& B, volatile
     prefetch_tmap(&p.tm_v);
     mbar_arrive_expect_tx(B.q_full, kTile);
     tma_load_3d(smem + kOffQ, &p.tm_q, B.q_full, 0, qtile * kBM, head);
-    const float* meta = p.v_meta + (int64_t)head * p.T * 256;
     int loaded = 0;
     for (int j = 0; j < p.T; ++j) {
         const int s = j % kStages, u = j / kStages;
         if (u > 0 && !mbar_wait(&B.kv_empty[s], (u - 1) & 1, abort)) break;
         uint8_t* st = smem + kOffStages + s * kStageBytes;
-        mbar_arrive_expect_tx(&B.kv_full[s], 2 * kTile + kMetaBytes);
+        mbar_arrive_expect_tx(&B.kv_full[s], 2 * kTile);
         tma_load_3d(st, &p.tm_k, &B.kv_full[s], 0, j * kBN, head);
         tma_load_3d(st + kTile, &p.tm_v, &B.kv_full[s], 0, j * 128, head);
-        bulk_load(st + 2 * kTile, meta + (int64_t)j * 256, kMetaBytes, &B.kv_full[s]);
         loaded = j + 1;
     }
     if (*abort) {   // no TMA write may land after the CTA exits
@@ -173,6 +178,23 @@ __device__ void producer(const Params& p, uint8_t* smem, const Bars& B, volatile
         for (int s = 0; s < kStages && s < loaded; ++s)     // last use of stage s: tile s + 4 u
             drain_wait(&B.kv_full[s], ((loaded - 1 - s) / kStages) & 1);
     }
+}
+
+// The per-tile V scales and means (1 KB) run on their own deeper ring, so a
+// K/V stage is free as soon as the PV of its tile has been committed.
+__device__ void meta_producer(const Params& p, uint8_t* smem, const Bars& B, volatile int* abort, int head) {
+    const float* meta = p.v_meta + (int64_t)head * p.T * 256;
+    int loaded = 0;
+    for (int j = 0; j < p.T; ++j) {
+        const int s = j % kMetaSlots, u = j / kMetaSlots;
+        if (u > 0 && !mbar_wait(&B.meta_empty[s], (u - 1) & 1, abort)) break;
+        mbar_arrive_expect_tx(&B.meta_full[s], kMetaBytes);
+        bulk_load(smem + kOffMeta + s * kMetaBytes, meta + (int64_t)j * 256, kMetaBytes, &B.meta_full[s]);
+        loaded = j + 1;
+    }
+    if (*abort)
+        for (int s = 0; s < kMetaSlots && s < loaded; ++s)
+            drain_wait(&B.meta_full[s], ((loaded - 1 - s) / kMetaSlots) & 1);
 }
 
 __device__ void mma_issuer(const Params& p, uint8_t* smem, const Bars& B, volatile int* abort, uint32_t tmem) {
@@ -198,6 +220,10 @@ __device__ void mma_issuer(const Params& p, uint8_t* smem, const Bars& B, volati
         // scores): keys 0-63 at columns 0-15, keys 64-127 at columns 64-79.
         if (!mbar_wait(&B.p_full[b], (j >> 1) & 1, abort)) break;
         if (j >= 2 && !mbar_wait(&B.o_free[b], ((j - 2) >> 1) & 1, abort)) break;
+        // K_{j+2} is waited for before PV_j, so that PV_j and QK_{j+2} reach
+        // the tensor pipe back to back
+        const int s2 = (j + 2) % kStages;
+        if (j + 2 < p.T && !mbar_wait(&B.kv_full[s2], ((j + 2) / kStages) & 1, abort)) break;
         tc_fence_after();
         const int s = j % kStages;
         const uint64_t vdesc = smem_desc_k128(smem + kOffStages + s * kStageBytes + kTile);
@@ -210,7 +236,12 @@ __device__ void mma_issuer(const Params& p, uint8_t* smem, const Bars& B, volati
         mma_commit(&B.kv_empty[s]);
         // QK_{j+2} overwrites S_j / P_j: the tensor pipe runs in issue order,
         // so it starts after PV_j has read P_j
-        if (j + 2 < p.T && !issue_qk(j + 2)) break;
+        if (j + 2 < p.T) {
+            const uint64_t kdesc = smem_desc_k128(smem + kOffStages + s2 * kStageBytes);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) mma_f8_ss(pa, qdesc + 2 * kk, kdesc + 2 * kk, idesc, kk > 0);
+            mma_commit(&B.s_full[b]);
+        }
     }
     mma_commit(B.drain);
     drain_wait(B.drain, 0);
@@ -345,9 +376,10 @@ __device__ void correction_role(const Params& p, uint8_t* smem, const Bars& B, v
     float den = 0.0f;
     bool done = true;
     for (int j = 0; j < p.T; ++j) {
-        const int b = j & 1, slot = j & 3, s = j % kStages;
+        const int b = j & 1, slot = j & 3, s = j % kMetaSlots;
         if (!mbar_wait(&B.o_full[b], (j >> 1) & 1, abort) ||
-            !mbar_wait(&B.st_full[slot], (j >> 2) & 1, abort)) {
+            !mbar_wait(&B.st_full[slot], (j >> 2) & 1, abort) ||
+            !mbar_wait(&B.meta_full[s], (j / kMetaSlots) & 1, abort)) {
             done = false;
             break;
         }
@@ -356,7 +388,7 @@ __device__ void correction_role(const Params& p, uint8_t* smem, const Bars& B, v
         const float M = __fadd_rn(st_mass[(slot * 2) * 128 + row], st_mass[(slot * 2 + 1) * 128 + row]);
         __syncwarp();
         mbar_arrive_if(&B.st_free[slot], lane == 0);
-        const float4* meta = reinterpret_cast<const float4*>(smem + kOffStages + s * kStageBytes + 2 * kTile);
+        const float4* meta = reinterpret_cast<const float4*>(smem + kOffMeta + s * kMetaBytes);
         const bool rescale = __any_sync(0xffffffffu, alpha != 1.0f);
         const float2 aa = make_float2(alpha, alpha), MM = make_float2(M, M);
         const uint32_t to = trow + kColO + b * 128 + c0;
@@ -392,7 +424,7 @@ __device__ void correction_role(const Params& p, uint8_t* smem, const Bars& B, v
         }
         den = __fadd_rn(__fmul_rn(alpha, den), M);
         __syncwarp();
-        mbar_arrive_if(&B.kv_empty[s], lane == 0);
+        mbar_arrive_if(&B.meta_empty[s], lane == 0);
     }
     if (!done) return;
     const int64_t grow = (int64_t)qtile * kBM + row;
@@ -446,7 +478,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
         mbar_init(B.q_full, 1);
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&B.kv_full[s], 1);
-            mbar_init(&B.kv_empty[s], 1 + 8);     // MMA commit + 8 correction warps
+            mbar_init(&B.kv_empty[s], 1);         // MMA commit after PV
+        }
+        for (int s = 0; s < kMetaSlots; ++s) {
+            mbar_init(&B.meta_full[s], 1);
+            mbar_init(&B.meta_empty[s], 8);       // 8 correction warps
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&B.s_full[b], 1);
@@ -478,6 +514,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
         reg_dealloc<32>();
         if (warp == 0 && lane == 0) producer(p, smem, B, abort, qtile, head);
         if (warp == 1 && lane == 0) mma_issuer(p, smem, B, abort, tmem);
+        if (warp == 2 && lane == 0) meta_producer(p, smem, B, abort, head);
     } else if (warp < 12) {
         softmax_role<EXPCAST>(p, smem, B, abort, tmem, qtile, head, warp & 3, (warp - 4) >> 2, lane);
     } else {

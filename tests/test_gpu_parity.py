@@ -306,6 +306,28 @@ def test_current_stream_is_used():
     assert m["relative_rmse"] <= RMSE_TOL
 
 
+@pytest.mark.parametrize("chunk_heads", [None, 2, 5])
+def test_streamed_host_attention_equals_device_attention(chunk_heads):
+    """attention_streamed (host tensors, transfers overlapped per head chunk)
+    gives the same bytes as attention on the whole device tensors: heads are
+    independent and every chunk runs the same forward.  Two steps with one
+    cache check the per-chunk layout refresh and reuse."""
+    from vc_attention_b200 import Config, LayoutCache, attention, attention_streamed
+    from vc_attention_b200.synthetic import make_qkv
+    cfg = Config(v_smooth=True, expcast=True)
+    q, k, v = make_qkv("c3", 5, heads=7, seq=1000)
+    hq, hk, hv = (x.pin_memory() for x in (q, k, v))
+    cache_h, cache_d = LayoutCache(cfg), LayoutCache(cfg)
+    for step in (0, 1):
+        got, stats = attention_streamed(hq, hk, hv, cfg, cache=cache_h, step=step, total_steps=8, request_id="r",
+                                        chunk_heads=chunk_heads)
+        want, _ = attention(q.cuda(), k.cuda(), v.cuda(), cfg, cache=cache_d, step=step, total_steps=8,
+                            request_id="r")
+        assert got.device.type == "cpu" and got.is_pinned()
+        assert torch.equal(got, want.cpu())
+        assert stats["layout_refreshed"] == (step == 0)
+
+
 def test_cache_refresh_reuse_and_window_with_native_clustering():
     """test_cuda.py:153-173: reused layout, current means, end of the window."""
     from vc_attention_b200 import Config, LayoutCache, attention

@@ -146,20 +146,31 @@ def forward(q, k, v, cfg, *, pi, active, scale, out=None, workspace=None, status
     with torch.cuda.device(q.device):
         _abi.check(lib, lib.vcb_forward(ctypes.byref(a), _stream(q.device)))
         if check_status:
-            flags = ctypes.c_int32(0)
-            _abi.check(lib, lib.vcb_read_status(status.data_ptr(), _stream(q.device), ctypes.byref(flags)))
-            if flags.value & _abi.FLAG_NONFINITE:
-                raise ValueError("Q/K/V must be finite")
-            if flags.value & _abi.FLAG_TIMEOUT:
-                raise RuntimeError("b200_fp8 attention kernel: a bounded device wait expired")
-            if flags.value & _abi.FLAG_INTERNAL:
-                raise RuntimeError("b200_fp8 attention kernel: device layout check failed")
+            raise_for_status(status)
     return out
 
 
+def raise_for_status(status):
+    """Reads the device status word (waits for the current stream) and raises
+    what the reference raises: ValueError for non-finite inputs, RuntimeError
+    for an expired device wait or a failed layout check."""
+    lib = _extension()
+    flags = ctypes.c_int32(0)
+    with torch.cuda.device(status.device):
+        _abi.check(lib, lib.vcb_read_status(status.data_ptr(), _stream(status.device), ctypes.byref(flags)))
+    if flags.value & _abi.FLAG_NONFINITE:
+        raise ValueError("Q/K/V must be finite")
+    if flags.value & _abi.FLAG_TIMEOUT:
+        raise RuntimeError("b200_fp8 attention kernel: a bounded device wait expired")
+    if flags.value & _abi.FLAG_INTERNAL:
+        raise RuntimeError("b200_fp8 attention kernel: device layout check failed")
+
+
 @torch.no_grad()
-def _attention(q, k, v, cfg, *, cache, step, total_steps, request_id, layer_id, scale):
-    """cuda_backend._attention (cuda_backend.py:26-66) for sm_100a."""
+def _attention(q, k, v, cfg, *, cache, step, total_steps, request_id, layer_id, scale, status=None):
+    """cuda_backend._attention (cuda_backend.py:26-66) for sm_100a.  With a
+    caller-owned ``status`` word the call does not wait for the device; the
+    caller reads the word later (raise_for_status) and owns the cache rollback."""
     from .core import LayoutCache
 
     _require_b200(q)
@@ -179,7 +190,8 @@ def _attention(q, k, v, cfg, *, cache, step, total_steps, request_id, layer_id, 
                                              layer_id=layer_id)
         qc, kc, vc = q.contiguous(), k.contiguous(), v.contiguous()
         try:
-            output = forward(qc, kc, vc, cfg, pi=pi, active=active, scale=scale)
+            output = forward(qc, kc, vc, cfg, pi=pi, active=active, scale=scale, status=status,
+                             check_status=status is None)
         except ValueError:
             cache._restore(snapshot, layer_id)
             raise

@@ -1,0 +1,112 @@
+"""Attention on host-resident Q/K/V: transfers overlapped with the forward.
+
+For callers whose activations live in (pinned) host memory, e.g. offloaded
+layers of a video DiT.  Heads are independent (the reference loops heads
+outermost, csrc/kernels.cu:313), so the B*H heads are cut into chunks and a
+three-stage pipeline runs over them on one GPU:
+
+    copy stream      H2D of Q/K/V for chunk i+1
+    compute stream   layout + quantisation + fused attention for chunk i
+    copy stream      D2H of the output of chunk i-1
+
+Two device input buffer sets alternate between chunks; events order the
+stages.
+The result is the same as ``attention`` on the whole tensors: every chunk
+runs the same forward on its heads, and the layout cache keeps one entry per
+chunk (key ``(layer_id, first_head)``) with the usual refresh schedule.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from .core import Config, LayoutCache, _validate
+
+
+def _chunks(n, size):
+    return [(a, min(a + size, n)) for a in range(0, n, size)]
+
+
+@torch.no_grad()
+def attention_streamed(q, k, v, config=None, *, cache=None, step=0, total_steps=1, request_id=None, layer_id=0,
+                       scale=None, device=None, chunk_heads=None, out=None, synchronize=True):
+    """``attention`` for BNSD tensors in host memory; returns (output on the
+    host, stats).  Pinned inputs (``tensor.pin_memory()``) let the copies
+    overlap the compute; ``out`` may be a preallocated pinned host tensor.
+    ``chunk_heads`` sets how many of the B*H heads go through the pipeline
+    at a time (default: an eighth of them).  With ``synchronize=False`` the
+    call returns once the work is queued (the output is complete when the
+    device's current stream reaches this point) and skips the check for
+    non-finite inputs."""
+    cfg = config or Config()
+    _validate(q, k, v, False, None)
+    if q.device.type != "cpu":
+        raise ValueError("attention_streamed takes host tensors; use attention for device tensors")
+    from .b200_backend import _attention, raise_for_status
+
+    device = torch.device(device if device is not None else "cuda")
+    b, h, sq, d = q.shape
+    sk, dv = k.shape[2], v.shape[3]
+    bh = b * h
+    qf, kf, vf = (x.reshape(bh, x.shape[2], x.shape[3]) for x in (q, k, v))
+    if out is None:
+        out = torch.empty((b, h, sq, dv), dtype=q.dtype, pin_memory=True)
+    elif out.shape != (b, h, sq, dv) or out.dtype != q.dtype or out.device.type != "cpu":
+        raise ValueError("out must be a host tensor of the output's shape and dtype")
+    of = out.view(bh, sq, dv)
+    size = chunk_heads or max(1, math.ceil(bh / 8))
+    parts = _chunks(bh, size)
+    if cache is None:
+        cache = LayoutCache(cfg)
+        request_id = "one-shot" if request_id is None else request_id
+    scale = d ** -0.5 if scale is None else scale
+
+    # One status word for all chunks, read once at the end: a per-chunk read
+    # would wait for the device and serialise the pipeline.  A failure rolls
+    # the whole cache back, as attention does for its one entry.
+    saved = (cache._request_id, dict(cache._states), {key: dict(val) for key, val in cache._states.items()})
+    with torch.cuda.device(device):
+        main = torch.cuda.current_stream()
+        status = torch.zeros(1, dtype=torch.int32, device=device)
+        h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
+        n = min(size, bh)
+        bufs = [tuple(torch.empty((1, n, s, w), dtype=q.dtype, device=device)
+                      for s, w in ((sq, d), (sk, d), (sk, dv))) for _ in range(2)]
+        in_ready = [torch.cuda.Event() for _ in range(2)]
+        in_free = [torch.cuda.Event() for _ in range(2)]
+        outs = [None, None]
+        stats = None
+        h2d.wait_stream(main)
+        for i, (a, e) in enumerate(parts):
+            s, m = i % 2, e - a
+            dq, dk, dvv = (t[:, :m] for t in bufs[s])
+            with torch.cuda.stream(h2d):
+                if i >= 2:
+                    h2d.wait_event(in_free[s])          # the forward of chunk i-2 is done with these buffers
+                dq.copy_(qf[a:e].unsqueeze(0), non_blocking=True)
+                dk.copy_(kf[a:e].unsqueeze(0), non_blocking=True)
+                dvv.copy_(vf[a:e].unsqueeze(0), non_blocking=True)
+                in_ready[s].record()
+            main.wait_event(in_ready[s])
+            res, stats = _attention(dq, dk, dvv, cfg, cache=cache, step=step, total_steps=total_steps,
+                                    request_id=request_id, layer_id=(layer_id, a), scale=scale, status=status)
+            in_free[s].record(main)
+            outs[s] = res
+            res.record_stream(d2h)
+            with torch.cuda.stream(d2h):
+                d2h.wait_stream(main)
+                of[a:e].copy_(res.view(m, sq, dv), non_blocking=True)
+        main.wait_stream(d2h)
+        main.wait_stream(h2d)
+        if synchronize:
+            try:
+                raise_for_status(status)
+            except ValueError:
+                cache._request_id, states, fields = saved
+                cache._states = states
+                for key, val in states.items():
+                    val.clear()
+                    val.update(fields[key])
+                raise
+    return out, dict(stats, streamed_chunks=len(parts))

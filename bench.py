@@ -314,6 +314,40 @@ def run_ours(args, world, rank, local):
         print(json.dumps(line))
 
 
+def run_case(args):
+    """Small single-GPU cases for profilers (ncu): `--case attn` runs the
+    fused attention on prepared operands, `--case prep` the clustering, Q/K
+    and V preparation, each `--steps` times at `--heads` heads of config 3."""
+    from vc_attention_b200 import stages
+    from vc_attention_b200.b200_backend import group_values
+    from vc_attention_b200.synthetic import make_qkv
+
+    q, k, v = make_qkv("c3", 1, device="cuda", heads=args.heads)
+    if args.case == "prep":
+        for _ in range(args.steps):
+            pi, _ = group_values(v, clusters=8, iterations=2)
+            stages.quantize_qk(q, k, pi=pi)
+            stages.prepare_v(v, pi=pi, active=True)
+        torch.cuda.synchronize()
+        print(json.dumps({"case": "prep", "heads": args.heads, "steps": args.steps}))
+        return
+    q8, qs, k8, ks = stages.quantize_qk(q, k)
+    v8, meta = stages.prepare_v(v, active=True)
+    del q, k, v
+    out = torch.empty((args.heads, S, D), dtype=torch.bfloat16, device="cuda")
+    times = []
+    for _ in range(args.steps):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        stages.attention_fp8(q8, qs, k8, ks, v8, meta, heads=args.heads, sq=S, sk=S, dv=D, expcast=True,
+                             has_mean=True, scale=D ** -0.5, out=out)
+        e.record()
+        e.synchronize()
+        times.append(s.elapsed_time(e))
+    print(json.dumps({"case": "attn", "heads": args.heads, "ms": times,
+                      "tflops": [flops(h=args.heads) / (t * 1e-3) / 1e12 for t in times]}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -321,7 +355,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--case", choices=("attn", "prep"), help="a small single-GPU case for profilers")
+    ap.add_argument("--heads", type=int, default=16, help="heads of the --case run")
     args = ap.parse_args()
+    if args.case:
+        run_case(args)
+        return
     world, rank, local = dist_setup()
     try:
         if args.impl == "reference":

@@ -193,7 +193,7 @@ __global__ void __launch_bounds__(256, 2) cluster_assign128_kernel(ClusterArgs a
     extern __shared__ __align__(16) uint8_t dsm[];
     uint8_t* xs = dsm;                                               // [256][RB], swizzled
     float* subs = reinterpret_cast<float*>(dsm + kChunk * RB);        // [8 warps][8 clusters][128]
-    __shared__ __align__(16) float cen[kMaxClusters * 128];
+    __shared__ __align__(16) float cen[kMaxClusters * 128];   // [c / 8][d][c % 8]
     __shared__ float cnorm[kMaxClusters];
     __shared__ uint8_t lab[kChunk];
     __shared__ int cnt[kMaxClusters];
@@ -204,8 +204,8 @@ __global__ void __launch_bounds__(256, 2) cluster_assign128_kernel(ClusterArgs a
     const int64_t base = (int64_t)chunk * kChunk;
     const int nvalid = (int)min((int64_t)kChunk, a.S - base);
     for (int i = tid; i < kMaxClusters * 128; i += 256) {
-        const int c = i / 128;
-        cen[i] = c < count ? a.centers[(h * count) * 128 + i] : 0.0f;
+        const int c = i / 128, d = i % 128;
+        cen[(c >> 3) * 1024 + d * 8 + (c & 7)] = c < count ? a.centers[(h * count) * 128 + i] : 0.0f;
     }
     if (tid < kMaxClusters) cnt[tid] = 0;
     const uint4* src = reinterpret_cast<const uint4*>(static_cast<const T*>(a.v) + (h * a.S + base) * 128);
@@ -230,7 +230,8 @@ __global__ void __launch_bounds__(256, 2) cluster_assign128_kernel(ClusterArgs a
     __syncthreads();
     if (tid < count) {
         float acc = 0.0f;
-        for (int d = 0; d < 128; ++d) acc = fmaf(cen[tid * 128 + d], cen[tid * 128 + d], acc);
+        const float* ct = cen + (tid >> 3) * 1024 + (tid & 7);
+        for (int d = 0; d < 128; ++d) acc = fmaf(ct[d * 8], ct[d * 8], acc);
         cnorm[tid] = acc;
     }
     __syncthreads();
@@ -241,9 +242,12 @@ __global__ void __launch_bounds__(256, 2) cluster_assign128_kernel(ClusterArgs a
         float xx = 0.0f, bestd = 0.0f;
         int best = 0;
         for (int c0 = 0; c0 < count; c0 += 8) {
-            float acc[8];
+            // two clusters per packed FMA: acc2[p] holds clusters c0 + 2p, c0 + 2p + 1;
+            // each cluster's chain still runs over d = 0..127 in order
+            const float* cg = cen + (c0 >> 3) * 1024;
+            float2 acc2[4];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+            for (int i = 0; i < 4; ++i) acc2[i] = make_float2(0.0f, 0.0f);
 #pragma unroll 2
             for (int k = 0; k < NCH; ++k) {
                 const uint4 raw = *reinterpret_cast<const uint4*>(xr + ((k ^ sw) << 4));
@@ -257,27 +261,24 @@ __global__ void __launch_bounds__(256, 2) cluster_assign128_kernel(ClusterArgs a
                     for (int e = 0; e < 8; ++e) x[e] = to_float(hv[e]);
                 }
 #pragma unroll
-                for (int e0 = 0; e0 < E; e0 += 4) {
-                    const int d = k * E + e0;
-                    if (c0 == 0) {
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) xx = fmaf(x[e0 + e], x[e0 + e], xx);
-                    }
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        const float4 cv = *reinterpret_cast<const float4*>(&cen[(c0 + i) * 128 + d]);
-                        acc[i] = fmaf(x[e0], cv.x, acc[i]);
-                        acc[i] = fmaf(x[e0 + 1], cv.y, acc[i]);
-                        acc[i] = fmaf(x[e0 + 2], cv.z, acc[i]);
-                        acc[i] = fmaf(x[e0 + 3], cv.w, acc[i]);
-                    }
+                for (int e = 0; e < E; ++e) {
+                    const int d = k * E + e;
+                    if (c0 == 0) xx = fmaf(x[e], x[e], xx);
+                    const float4 ca = *reinterpret_cast<const float4*>(cg + d * 8);
+                    const float4 cb = *reinterpret_cast<const float4*>(cg + d * 8 + 4);
+                    const float2 x2 = make_float2(x[e], x[e]);
+                    acc2[0] = ffma2(x2, make_float2(ca.x, ca.y), acc2[0]);
+                    acc2[1] = ffma2(x2, make_float2(ca.z, ca.w), acc2[1]);
+                    acc2[2] = ffma2(x2, make_float2(cb.x, cb.y), acc2[2]);
+                    acc2[3] = ffma2(x2, make_float2(cb.z, cb.w), acc2[3]);
                 }
             }
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
                 const int c = c0 + i;
                 if (c < count) {
-                    const float dist = __fsub_rn(__fadd_rn(xx, cnorm[c]), __fmul_rn(2.0f, acc[i]));
+                    const float dot = (i & 1) ? acc2[i >> 1].y : acc2[i >> 1].x;
+                    const float dist = __fsub_rn(__fadd_rn(xx, cnorm[c]), __fmul_rn(2.0f, dot));
                     if (c == 0 || dist < bestd) { bestd = dist; best = c; }
                 }
             }

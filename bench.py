@@ -314,6 +314,59 @@ def run_ours(args, world, rank, local):
         print(json.dumps(line))
 
 
+def run_ulysses(args, world, rank, local):
+    """Configuration 4 on N GPUs: B1 H24 S131072 D128 bf16, combined mode,
+    inputs sequence-sharded (S/N tokens of all heads per rank).  A step is the
+    seq->head all-to-all of Q/K/V, the forward on 24/N heads over all tokens,
+    and the head->seq all-to-all of the output.  Prints one JSON line (rank 0)
+    with the step time (max over ranks) and the share of the all-to-alls."""
+    from vc_attention_b200 import Config, sharding
+    from vc_attention_b200.synthetic import make_qkv
+
+    heads, seq = 24, 131072
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    q, k, v = make_qkv("c4", 2000, device=device)
+    s = seq // world
+    q, k, v = (x[:, :, rank * s:(rank + 1) * s].contiguous() for x in (q, k, v))
+    torch.cuda.empty_cache()
+    cfg = Config(v_smooth=True, expcast=True)
+    group = torch.distributed.group.WORLD if world > 1 else None
+
+    def step():
+        if world == 1:
+            from vc_attention_b200 import attention
+            return attention(q, k, v, cfg)[0]
+        return sharding.attention_seq_sharded(q, k, v, cfg, group=group)[0]
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record()
+    for _ in range(args.steps):
+        step()
+    e0.record()
+    e0.synchronize()
+    ms = sharding.max_over_ranks(s0.elapsed_time(e0) / args.steps)
+    a2a_ms = 0.0
+    if world > 1:   # the two all-to-alls alone
+        s1, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s1.record()
+        for _ in range(args.steps):
+            hs = [sharding.seq_to_heads(x, group) for x in (q, k, v)]
+            sharding.heads_to_seq(hs[0], group)
+        e1.record()
+        e1.synchronize()
+        a2a_ms = sharding.max_over_ranks(s1.elapsed_time(e1) / args.steps)
+    if rank == 0:
+        total = 4.0 * heads * seq * seq * 128
+        print(json.dumps({"case": "ulysses", "workload": "c4: B1 H24 S131072 D128 bf16 combined, sequence-sharded",
+                          "n_gpus": world, "steps": args.steps, "ms_per_step": ms,
+                          "tflops_total": total / (ms * 1e-3) / 1e12, "all_to_all_ms": a2a_ms}))
+
+
 def run_case(args):
     """Small single-GPU cases for profilers (ncu): `--case attn` runs the
     fused attention on prepared operands, `--case prep` the clustering, Q/K
@@ -355,15 +408,18 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--case", choices=("attn", "prep"), help="a small single-GPU case for profilers")
+    ap.add_argument("--case", choices=("attn", "prep", "ulysses"),
+                    help="attn / prep: small single-GPU cases for profilers; ulysses: config 4 sequence-sharded")
     ap.add_argument("--heads", type=int, default=16, help="heads of the --case run")
     args = ap.parse_args()
-    if args.case:
+    if args.case in ("attn", "prep"):
         run_case(args)
         return
     world, rank, local = dist_setup()
     try:
-        if args.impl == "reference":
+        if args.case == "ulysses":
+            run_ulysses(args, world, rank, local)
+        elif args.impl == "reference":
             run_reference(args, world, rank)
         else:
             run_ours(args, world, rank, local)

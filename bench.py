@@ -279,7 +279,7 @@ def run_ours(args, world, rank, local):
         barrier(world)
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
-        # host in, host out: per-chunk H2D / forward / D2H overlapped on three streams
+        # host in, host out: per-chunk H2D, forwards on rotating compute streams, D2H
         attention_streamed(hq, hk, hv, cfg, cache=LayoutCache(cfg), step=0, total_steps=50, request_id=i,
                            device=device, out=hout, synchronize=False)
         e.record()

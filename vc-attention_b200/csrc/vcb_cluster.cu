@@ -336,8 +336,8 @@ __global__ void __launch_bounds__(256, 2) cluster_assign128_kernel(ClusterArgs a
     if (tid < count) a.pcnt[((int64_t)h * a.nchunk + chunk) * count + tid] = cnt[tid];
 }
 
-// One CTA per (head, cluster), thread d per channel; chunks added in order
-// (the loads are independent, only the adds are chained).
+// One CTA per (head, cluster), thread d per channel; chunks added in order.
+// The loads are independent (32 in flight per thread), only the adds chain.
 __global__ void __launch_bounds__(128) cluster_update_kernel(ClusterArgs a) {
     const int64_t h = blockIdx.x;
     const int c = blockIdx.y, d = threadIdx.x;
@@ -347,39 +347,75 @@ __global__ void __launch_bounds__(128) cluster_update_kernel(ClusterArgs a) {
     const int64_t stride = (int64_t)a.count * 128;
     float total = 0.0f;
     long long n = 0;
-#pragma unroll 8
-    for (int ch = 0; ch < a.nchunk; ++ch) {
-        total += __ldg(src + ch * stride);
-        n += __ldg(cnt + (int64_t)ch * a.count);
+    for (int ch0 = 0; ch0 < a.nchunk; ch0 += 32) {
+        float x[32];
+        int k[32];
+#pragma unroll
+        for (int u = 0; u < 32; ++u) {
+            const bool in = ch0 + u < a.nchunk;
+            x[u] = in ? __ldg(src + (ch0 + u) * stride) : 0.0f;
+            k[u] = in ? __ldg(cnt + (int64_t)(ch0 + u) * a.count) : 0;
+        }
+#pragma unroll
+        for (int u = 0; u < 32; ++u) {
+            if (ch0 + u < a.nchunk) total += x[u];
+            n += k[u];
+        }
     }
     if (n > 0) a.centers[(h * a.count + c) * a.D + d] = total / (float)n;
 }
 
-__global__ void cluster_offsets_kernel(ClusterArgs a) {
+// Exclusive prefix of the per-(cluster, chunk) counts in cluster-major,
+// chunk-minor order: one CTA per head, each thread a contiguous run of that
+// order, the run totals scanned across warps (integer sums: any order).
+__global__ void __launch_bounds__(256) cluster_offsets_kernel(ClusterArgs a) {
+    __shared__ int wsum[8];
     const int64_t h = blockIdx.x;
-    if (threadIdx.x != 0) return;
-    int running = 0;
-    for (int c = 0; c < a.count; ++c)
-        for (int ch = 0; ch < a.nchunk; ++ch) {
-            const int64_t i = ((int64_t)h * a.nchunk + ch) * a.count + c;
-            a.off[i] = running;
-            running += a.pcnt[i];
-        }
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int len = a.count * a.nchunk;
+    const int per = (len + 255) / 256;
+    const int q0 = min(tid * per, len), q1 = min(q0 + per, len);
+    auto at = [&](int q) { return ((int64_t)h * a.nchunk + q % a.nchunk) * a.count + q / a.nchunk; };
+    int mine = 0;
+    for (int q = q0; q < q1; ++q) mine += a.pcnt[at(q)];
+    int incl = mine;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+    }
+    if (lane == 31) wsum[warp] = incl;
+    __syncthreads();
+    int run = incl - mine;
+    for (int w = 0; w < warp; ++w) run += wsum[w];
+    for (int q = q0; q < q1; ++q) {
+        const int64_t i = at(q);
+        const int c = a.pcnt[i];
+        a.off[i] = run;
+        run += c;
+    }
 }
 
+// Stable counting-sort scatter: the rank of token j among the chunk's
+// earlier tokens of its cluster = rank inside its warp (match mask) plus the
+// counts of the warps before it.
 __global__ void __launch_bounds__(256) cluster_scatter_kernel(ClusterArgs a) {
-    __shared__ uint8_t lab[kChunk];
+    __shared__ int wcnt[8][kMaxClusters];
     const int64_t h = blockIdx.y;
     const int chunk = blockIdx.x;
     const int64_t base = (int64_t)chunk * kChunk;
     const int nvalid = (int)min((int64_t)kChunk, a.S - base);
-    const int j = threadIdx.x;
-    if (j < nvalid) lab[j] = a.labels[h * a.S + base + j];
+    const int j = threadIdx.x, warp = j >> 5, lane = j & 31;
+    for (int i = j; i < 8 * kMaxClusters; i += 256) (&wcnt[0][0])[i] = 0;
     __syncthreads();
-    if (j >= nvalid) return;
-    const int c = lab[j];
-    int rank = 0;
-    for (int i = 0; i < j; ++i) rank += lab[i] == c;
+    const int c = j < nvalid ? a.labels[h * a.S + base + j] : -1;
+    const unsigned same = __match_any_sync(0xffffffffu, c);
+    const int rank_in_warp = __popc(same & ((1u << lane) - 1u));
+    if (c >= 0 && rank_in_warp == 0) wcnt[warp][c] = __popc(same);
+    __syncthreads();
+    if (c < 0) return;
+    int rank = rank_in_warp;
+    for (int w = 0; w < warp; ++w) rank += wcnt[w][c];
     const int dst = a.off[((int64_t)h * a.nchunk + chunk) * a.count + c] + rank;
     a.pi[h * a.S + dst] = (int32_t)(base + j);
 }
@@ -431,7 +467,7 @@ int run(const vcb_group_args* p, cudaStream_t st) {
         cluster_update_kernel<<<dim3((unsigned)p->heads, (unsigned)count), 128, 0, st>>>(a);
         VCB_CUDA(cudaGetLastError());
     }
-    cluster_offsets_kernel<<<(unsigned)p->heads, 32, 0, st>>>(a);
+    cluster_offsets_kernel<<<(unsigned)p->heads, 256, 0, st>>>(a);
     VCB_CUDA(cudaGetLastError());
     cluster_scatter_kernel<<<dim3(nchunk, (unsigned)p->heads), 256, 0, st>>>(a);
     VCB_CUDA(cudaGetLastError());

@@ -76,6 +76,14 @@ def group_values(v, *, clusters, iterations, centers=None):
     return native(v, clusters=clusters, iterations=iterations, centers=centers)
 
 
+def _mark_use(t):
+    """Tell the caching allocator that ``t`` is used on the current stream, so
+    that a cached layout made on one stream and read on another is not handed
+    out again before that stream is done with it."""
+    if t is not None and t.is_cuda:
+        t.record_stream(torch.cuda.current_stream(t.device))
+
+
 class LayoutCache:
     """Request-scoped layout state (core.py:166-211). Callers must supply a real request identifier."""
 
@@ -122,6 +130,8 @@ class LayoutCache:
         active = self.config.v_smooth and step < math.ceil(total_steps * self.config.active_fraction)
         refresh = active and (state is None or step - state["refresh_step"] >= self.config.refresh_interval)
         if refresh:
+            if state is not None:
+                _mark_use(state["centers"])
             pi, centers = group_values(
                 v,
                 clusters=self.config.clusters,
@@ -132,6 +142,7 @@ class LayoutCache:
             self._states[layer_id] = state
         if state is not None:
             state["step"] = step
+            _mark_use(state["pi"])
         return (None if state is None else state["pi"]), active, refresh
 
 

@@ -3,14 +3,17 @@
 For callers whose activations live in (pinned) host memory, e.g. offloaded
 layers of a video DiT.  Heads are independent (the reference loops heads
 outermost, csrc/kernels.cu:313), so the B*H heads are cut into chunks and a
-three-stage pipeline runs over them on one GPU:
+pipeline runs over them on one GPU:
 
-    copy stream      H2D of Q/K/V for chunk i+1
-    compute stream   layout + quantisation + fused attention for chunk i
-    copy stream      D2H of the output of chunk i-1
+    copy stream        H2D of Q/K/V, chunk after chunk, into a ring of
+                       device input buffers
+    compute streams    layout + quantisation + fused attention; chunks take
+                       the compute streams in turn, so the small launches and
+                       the last partial wave of one chunk overlap the next
+    copy stream        D2H of each chunk's output once its forward is done
 
-Two device input buffer sets alternate between chunks; events order the
-stages.
+Events order the stages; a buffer set is refilled once the forward that read
+it is done.  The streams are made once per device and reused.
 The result is the same as ``attention`` on the whole tensors: every chunk
 runs the same forward on its heads, and the layout cache keeps one entry per
 chunk (key ``(layer_id, first_head)``) with the usual refresh schedule.
@@ -24,8 +27,24 @@ import torch
 from .core import Config, LayoutCache, _validate
 
 
+_BUFFER_SETS = 8          # device input buffer sets in the ring
+_COMPUTE_STREAMS = 3      # compute streams the chunks rotate over
+_streams = {}
+
+
 def _chunks(n, size):
     return [(a, min(a + size, n)) for a in range(0, n, size)]
+
+
+def _pipeline_streams(device):
+    """(h2d, d2h, [compute...]) for ``device``, made once and reused, so the
+    caching allocator keeps serving the same per-stream pools."""
+    key = device.index if device.index is not None else torch.cuda.current_device()
+    if key not in _streams:
+        with torch.cuda.device(key):
+            _streams[key] = (torch.cuda.Stream(), torch.cuda.Stream(),
+                             [torch.cuda.Stream() for _ in range(_COMPUTE_STREAMS)])
+    return _streams[key]
 
 
 @torch.no_grad()
@@ -35,10 +54,10 @@ def attention_streamed(q, k, v, config=None, *, cache=None, step=0, total_steps=
     host, stats).  Pinned inputs (``tensor.pin_memory()``) let the copies
     overlap the compute; ``out`` may be a preallocated pinned host tensor.
     ``chunk_heads`` sets how many of the B*H heads go through the pipeline
-    at a time (default: a tenth of them).  With ``synchronize=False`` the
-    call returns once the work is queued (the output is complete when the
-    device's current stream reaches this point) and skips the check for
-    non-finite inputs."""
+    at a time (default: a fortieth of them, at least one).  With
+    ``synchronize=False`` the call returns once the work is queued (the
+    output is complete when the device's current stream reaches this point)
+    and skips the check for non-finite inputs."""
     cfg = config or Config()
     _validate(q, k, v, False, None)
     if q.device.type != "cpu":
@@ -55,7 +74,7 @@ def attention_streamed(q, k, v, config=None, *, cache=None, step=0, total_steps=
     elif out.shape != (b, h, sq, dv) or out.dtype != q.dtype or out.device.type != "cpu":
         raise ValueError("out must be a host tensor of the output's shape and dtype")
     of = out.view(bh, sq, dv)
-    size = chunk_heads or max(1, math.ceil(bh / 10))
+    size = chunk_heads or max(1, math.ceil(bh / 40))
     parts = _chunks(bh, size)
     if cache is None:
         cache = LayoutCache(cfg)
@@ -69,34 +88,42 @@ def attention_streamed(q, k, v, config=None, *, cache=None, step=0, total_steps=
     with torch.cuda.device(device):
         main = torch.cuda.current_stream()
         status = torch.zeros(1, dtype=torch.int32, device=device)
-        h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
+        h2d, d2h, compute = _pipeline_streams(device)
         n = min(size, bh)
+        nbuf = min(_BUFFER_SETS, len(parts))
         bufs = [tuple(torch.empty((1, n, s, w), dtype=q.dtype, device=device)
-                      for s, w in ((sq, d), (sk, d), (sk, dv))) for _ in range(2)]
-        in_ready = [torch.cuda.Event() for _ in range(2)]
-        in_free = [torch.cuda.Event() for _ in range(2)]
-        outs = [None, None]
+                      for s, w in ((sq, d), (sk, d), (sk, dv))) for _ in range(nbuf)]
+        for t in (x for buf in bufs for x in buf):
+            for c in (h2d, *compute):
+                t.record_stream(c)
+        in_ready = [torch.cuda.Event() for _ in range(nbuf)]
+        in_free = [torch.cuda.Event() for _ in range(nbuf)]
         stats = None
         h2d.wait_stream(main)
+        for c in compute:
+            c.wait_stream(main)
         for i, (a, e) in enumerate(parts):
-            s, m = i % 2, e - a
+            s, m = i % nbuf, e - a
             dq, dk, dvv = (t[:, :m] for t in bufs[s])
             with torch.cuda.stream(h2d):
-                if i >= 2:
-                    h2d.wait_event(in_free[s])          # the forward of chunk i-2 is done with these buffers
+                if i >= nbuf:
+                    h2d.wait_event(in_free[s])          # the forward of chunk i-nbuf is done with these buffers
                 dq.copy_(qf[a:e].unsqueeze(0), non_blocking=True)
                 dk.copy_(kf[a:e].unsqueeze(0), non_blocking=True)
                 dvv.copy_(vf[a:e].unsqueeze(0), non_blocking=True)
                 in_ready[s].record()
-            main.wait_event(in_ready[s])
-            res, stats = _attention(dq, dk, dvv, cfg, cache=cache, step=step, total_steps=total_steps,
-                                    request_id=request_id, layer_id=(layer_id, a), scale=scale, status=status)
-            in_free[s].record(main)
-            outs[s] = res
-            res.record_stream(d2h)
+            cs = compute[i % len(compute)]
+            with torch.cuda.stream(cs):
+                cs.wait_event(in_ready[s])
+                res, stats = _attention(dq, dk, dvv, cfg, cache=cache, step=step, total_steps=total_steps,
+                                        request_id=request_id, layer_id=(layer_id, a), scale=scale, status=status)
+                in_free[s].record(cs)
+                res.record_stream(d2h)
             with torch.cuda.stream(d2h):
-                d2h.wait_stream(main)
+                d2h.wait_stream(cs)
                 of[a:e].copy_(res.view(m, sq, dv), non_blocking=True)
+        for c in compute:
+            main.wait_stream(c)
         main.wait_stream(d2h)
         main.wait_stream(h2d)
         if synchronize:

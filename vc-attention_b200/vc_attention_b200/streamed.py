@@ -13,7 +13,10 @@ pipeline runs over them on one GPU:
     copy stream        D2H of each chunk's output once its forward is done
 
 Events order the stages; a buffer set is refilled once the forward that read
-it is done.  The streams are made once per device and reused.
+it is done.  The ring is one allocation per input, and the streams are made
+once per device and reused, so repeated calls take the same blocks from the
+caching allocator.  (A ring as large as the inputs, 1 GB at configuration 3,
+made repeated calls stall on fresh device allocations.)
 The result is the same as ``attention`` on the whole tensors: every chunk
 runs the same forward on its heads, and the layout cache keeps one entry per
 chunk (key ``(layer_id, first_head)``) with the usual refresh schedule.
@@ -27,7 +30,7 @@ import torch
 from .core import Config, LayoutCache, _validate
 
 
-_BUFFER_SETS = 8          # device input buffer sets in the ring
+_BUFFER_SETS = 8          # chunk-sized input sets in the device ring
 _COMPUTE_STREAMS = 3      # compute streams the chunks rotate over
 _streams = {}
 
@@ -90,12 +93,13 @@ def attention_streamed(q, k, v, config=None, *, cache=None, step=0, total_steps=
         status = torch.zeros(1, dtype=torch.int32, device=device)
         h2d, d2h, compute = _pipeline_streams(device)
         n = min(size, bh)
-        nbuf = min(_BUFFER_SETS, len(parts))
-        bufs = [tuple(torch.empty((1, n, s, w), dtype=q.dtype, device=device)
-                      for s, w in ((sq, d), (sk, d), (sk, dv))) for _ in range(nbuf)]
-        for t in (x for buf in bufs for x in buf):
+        shapes = ((sq, d), (sk, d), (sk, dv))
+        nbuf = min(len(parts), _BUFFER_SETS)
+        ring = [torch.empty((nbuf * n, x, y), dtype=q.dtype, device=device) for x, y in shapes]
+        for t in ring:
             for c in (h2d, *compute):
                 t.record_stream(c)
+        bufs = [tuple(t[i * n:(i + 1) * n].unsqueeze(0) for t in ring) for i in range(nbuf)]
         in_ready = [torch.cuda.Event() for _ in range(nbuf)]
         in_free = [torch.cuda.Event() for _ in range(nbuf)]
         stats = None

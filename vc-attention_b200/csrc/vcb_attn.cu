@@ -12,8 +12,8 @@
 //   warp 1      MMA issuer (one thread): S_j = Q8 K8_j^T into TMEM
 //               (tcgen05.mma kind::f8f6f4, E4M3 x E4M3 -> F32) and
 //               O_j = P_j R_j with P_j in TMEM and R_j in shared memory.
-//   warps 4-11  softmax, two threads per query row (64 scores each; the
-//               halves exchange their partial row maxima): row max, alpha,
+//   warps 4-11  softmax, two threads of one warp per query row (64 scores
+//               each; one shuffle swaps the partial row maxima): row max, alpha,
 //               the ExpCast byte encode (one packed FMA per pair of scores;
 //               the f16-subnormal conversion rounds to the integer code and
 //               clamps it at zero) or exp + E4M3(p * 256); the row mass;
@@ -54,8 +54,7 @@ constexpr uint32_t kOffQ = 0;
 constexpr uint32_t kOffStages = kTile;
 constexpr uint32_t kOffMeta = kOffStages + kStages * kStageBytes;    // vscale[128], mu[128] per slot
 constexpr uint32_t kOffStats = kOffMeta + kMetaSlots * kMetaBytes;   // alpha[4][128], mass[4][2][128]
-constexpr uint32_t kOffXmax = kOffStats + 3 * 4 * 128 * 4;            // {tile + 1, partial max} [2][2][128]
-constexpr uint32_t kOffBars = kOffXmax + 2 * 2 * 128 * 8;
+constexpr uint32_t kOffBars = kOffStats + 3 * 4 * 128 * 4;
 constexpr int kNumBars = 1 + 2 * kStages + 2 * kMetaSlots + 2 * 4 + 2 * 4 + 1;
 constexpr uint32_t kOffMisc = kOffBars + kNumBars * 8;
 constexpr uint32_t kSmemBytes = kOffMisc + 16;
@@ -128,32 +127,6 @@ __device__ __forceinline__ uint32_t cvt_relu_f16x2(float hi, float lo) {
     uint32_t d;
     asm("cvt.rn.relu.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
     return d;
-}
-
-__device__ __forceinline__ void st_volatile_u64(uint64_t* p, uint64_t v) {
-    asm volatile("st.volatile.shared.u64 [%0], %1;" ::"r"(smem_u32(p)), "l"(v) : "memory");
-}
-
-// Waits until the 64-bit word at p carries `tag` in its upper half and
-// returns its lower half as a float.  Gives up (false) when the CTA aborts or
-// after kWaitLimitNs, setting the abort flag.
-__device__ __forceinline__ bool spin_tagged(const uint64_t* p, uint32_t tag, volatile int* abort, float& val) {
-    const uint32_t a = smem_u32(p);
-    uint64_t v;
-    asm volatile("ld.volatile.shared.u64 %0, [%1];" : "=l"(v) : "r"(a) : "memory");
-    if ((uint32_t)(v >> 32) != tag) {
-        const uint64_t t0 = globaltimer();
-        for (uint32_t i = 1;; ++i) {
-            asm volatile("ld.volatile.shared.u64 %0, [%1];" : "=l"(v) : "r"(a) : "memory");
-            if ((uint32_t)(v >> 32) == tag) break;
-            if ((i & 31u) == 0) {
-                if (*abort) return false;
-                if (globaltimer() - t0 > kWaitLimitNs) { *abort = 1; return false; }
-            }
-        }
-    }
-    val = __uint_as_float((uint32_t)v);
-    return true;
 }
 
 __device__ void producer(const Params& p, uint8_t* smem, const Bars& B, volatile int* abort, int qtile,
@@ -247,14 +220,46 @@ __device__ void mma_issuer(const Params& p, uint8_t* smem, const Bars& B, volati
     drain_wait(B.drain, 0);
 }
 
-// Two threads per query row: warps 4-7 own columns [0, 64) of the S tile,
-// warps 8-11 columns [64, 128), each warp the TMEM lane quarter warp % 4.
-// The halves exchange their partial row maxima through shared memory and a
-// per-quarter mbarrier (bounded wait, so a timed-out partner cannot hang it).
+// Two threads of one warp per query row: warp w (quarter w % 4, sub (w-4)/4)
+// owns TMEM lanes 32*quarter + 16*sub + [0, 16); lane t < 16 reads columns
+// [0, 64) of its row and lane t + 16 columns [64, 128), so the partial row
+// maxima meet in one shuffle.
+
+// 16 TMEM lanes x 32 columns per half: thread t < 16 reads lane base + t at
+// columns [c, c + 32), thread t + 16 the same lane at [c + 64, c + 96)
+// (tcgen05 .16x32bx2 with a half split of 64 columns).
+template <int OFF, int N>
+__device__ __forceinline__ void tmem_ld16x2_at(uint32_t taddr, uint32_t (&r)[N]) {
+    static_assert(OFF + 32 <= N, "range");
+    asm volatile(
+        "tcgen05.ld.sync.aligned.16x32bx2.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32], 64;"
+        : "=r"(r[OFF + 0]), "=r"(r[OFF + 1]), "=r"(r[OFF + 2]), "=r"(r[OFF + 3]), "=r"(r[OFF + 4]),
+          "=r"(r[OFF + 5]), "=r"(r[OFF + 6]), "=r"(r[OFF + 7]), "=r"(r[OFF + 8]), "=r"(r[OFF + 9]),
+          "=r"(r[OFF + 10]), "=r"(r[OFF + 11]), "=r"(r[OFF + 12]), "=r"(r[OFF + 13]), "=r"(r[OFF + 14]),
+          "=r"(r[OFF + 15]), "=r"(r[OFF + 16]), "=r"(r[OFF + 17]), "=r"(r[OFF + 18]), "=r"(r[OFF + 19]),
+          "=r"(r[OFF + 20]), "=r"(r[OFF + 21]), "=r"(r[OFF + 22]), "=r"(r[OFF + 23]), "=r"(r[OFF + 24]),
+          "=r"(r[OFF + 25]), "=r"(r[OFF + 26]), "=r"(r[OFF + 27]), "=r"(r[OFF + 28]), "=r"(r[OFF + 29]),
+          "=r"(r[OFF + 30]), "=r"(r[OFF + 31])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st16x2_16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.16x32bx2.x16.b32 [%0], 64, {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
+        "%13, %14, %15, %16};"
+        ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+          "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+
 template <bool EXPCAST>
 __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, volatile int* abort, uint32_t tmem,
-                             int qtile, int head, int quarter, int hs, int lane) {
-    const int row = quarter * 32 + lane;
+                             int qtile, int head, int quarter, int sub, int lane) {
+    // warp (quarter, sub) owns rows quarter*32 + sub*16 + [0, 16); lanes t and
+    // t + 16 share row t, columns [0, 64) and [64, 128)
+    const int hs = lane >> 4;
+    const int row = quarter * 32 + sub * 16 + (lane & 15);
     const int64_t grow = (int64_t)qtile * kBM + row;
     int qb = (int)(grow / p.q_block);
     if (qb >= p.nqb) qb = p.nqb - 1;
@@ -262,8 +267,7 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, vola
     const float* ksp = p.k_scale + (int64_t)head * p.nkb;
     float* st_alpha = reinterpret_cast<float*>(smem + kOffStats);
     float* st_mass = st_alpha + 4 * 128;                       // [4][2][128]
-    uint64_t* xmax = reinterpret_cast<uint64_t*>(smem + kOffXmax);   // [2][2][128]
-    const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16) + 64 * hs;
+    const uint32_t trow = tmem + ((uint32_t)(quarter * 32 + sub * 16) << 16);
     const int kstep = p.kq / kBN;
     int kidx = 0, kcnt = 0;
     float m = -INFINITY;
@@ -278,8 +282,8 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, vola
         tc_fence_after();
         uint32_t r[64];
         const uint32_t ts = trow + kColS + b * kBN;
-        tmem_ld32_at<0>(ts, r);
-        tmem_ld32_at<32>(ts + 32, r);
+        tmem_ld16x2_at<0>(ts, r);
+        tmem_ld16x2_at<32>(ts + 32, r);
         tmem_wait_ld();
         const int nvalid = (int)min((int64_t)kBN, p.sk - (int64_t)j * kBN) - 64 * hs;
         if (nvalid < 64) {
@@ -296,12 +300,7 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, vola
             for (int k = 0; k < 4; ++k)
                 mx[k] = fmax3(mx[k], __uint_as_float(r[8 * t + 2 * k]), __uint_as_float(r[8 * t + 2 * k + 1]));
         const float pmax = fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]);
-        // The two halves of a row swap partial maxima through one 64-bit
-        // word each: {tile + 1, max}, written and read whole, so the tag
-        // says when the value is there (bounded spin).
-        st_volatile_u64(&xmax[(b * 2 + hs) * 128 + row], ((uint64_t)(j + 1) << 32) | __float_as_uint(pmax));
-        float omax;
-        if (!spin_tagged(&xmax[(b * 2 + (hs ^ 1)) * 128 + row], (uint32_t)(j + 1), abort, omax)) break;
+        const float omax = __shfl_xor_sync(0xffffffffu, pmax, 16);   // the other half of the row
         const float rmax = fmaxf(pmax, omax);
         const float c = __fmul_rn(__fmul_rn(qs_scale, ks), p.scale);
         const float m_new = fmaxf(m, __fmul_rn(rmax, c));
@@ -348,7 +347,7 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, vola
         if (EXPCAST) M = __fmul_rn(M, 256.0f);
         // P_j over this thread's own (already read) S_j columns: 4 codes per
         // 32-bit column, the A-operand layout of the PV MMA
-        tmem_st16(ts, pk);
+        tmem_st16x2_16(ts, pk);
         const int slot = j & 3;
         if (j >= 4 && !mbar_wait(&B.st_free[slot], ((j >> 2) - 1) & 1, abort)) break;
         if (hs == 0) st_alpha[slot * 128 + row] = alpha;
@@ -472,8 +471,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int qtile = blockIdx.x, head = blockIdx.y;
 
-    for (int i = threadIdx.x; i < 2 * 2 * 128; i += kThreads)
-        reinterpret_cast<uint64_t*>(smem + kOffXmax)[i] = 0;
     if (threadIdx.x == 0) {
         mbar_init(B.q_full, 1);
         for (int s = 0; s < kStages; ++s) {

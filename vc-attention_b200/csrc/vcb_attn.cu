@@ -26,7 +26,8 @@
 // 512 columns).  P_j lives in S_j's columns, so the MMA issues PV_j and then
 // QK_{j+2} into the same buffer (the tensor pipe keeps issue order); QK_{j+2}
 // runs while the softmax works on tile j+1.  PV_j only waits for the
-// correction of tile j-2.
+// correction of tile j-2.  The commit that signals PV_j done (o_full) also
+// tells the producer that K/V stage j % 4 is free.
 //
 // Numerical contract (core.py:307-341): S = (q8 . k8) * qs * ks * scale;
 // ExpCast code = rne(clamp(fma(S - m, 8 log2 e, 119.65), 0, 120)) viewed as
@@ -37,6 +38,7 @@
 // den); 256 is a power of two, so no rounding changes.  Every mbarrier wait
 // is bounded (vcb_common.cuh).
 #include "vcb_internal.h"
+#include <type_traits>
 
 namespace vcb {
 
@@ -55,7 +57,7 @@ constexpr uint32_t kOffStages = kTile;
 constexpr uint32_t kOffMeta = kOffStages + kStages * kStageBytes;    // vscale[128], mu[128] per slot
 constexpr uint32_t kOffStats = kOffMeta + kMetaSlots * kMetaBytes;   // alpha[4][128], mass[4][2][128]
 constexpr uint32_t kOffBars = kOffStats + 3 * 4 * 128 * 4;
-constexpr int kNumBars = 1 + 2 * kStages + 2 * kMetaSlots + 2 * 4 + 2 * 4 + 1;
+constexpr int kNumBars = 1 + kStages + 2 * kMetaSlots + 2 * 4 + 2 * 4 + 1;
 constexpr uint32_t kOffMisc = kOffBars + kNumBars * 8;
 constexpr uint32_t kSmemBytes = kOffMisc + 16;
 constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;
@@ -84,12 +86,11 @@ struct Params {
 struct Bars {
     uint64_t* q_full;
     uint64_t* kv_full;     // [kStages]
-    uint64_t* kv_empty;    // [kStages]     PV of the stage's tile committed
     uint64_t* meta_full;   // [kMetaSlots]
     uint64_t* meta_empty;  // [kMetaSlots]  the 8 correction warps have read the slot
     uint64_t* s_full;      // [2]  QK_j done
     uint64_t* p_full;      // [2]  P_j in TMEM (implies S_j fully read)
-    uint64_t* o_full;      // [2]  PV_j done
+    uint64_t* o_full;      // [2]  PV_j done; also frees K/V stage j % kStages
     uint64_t* o_free;      // [2]  correction has read O_j
     uint64_t* st_full;     // [4]  alpha / mass of tile j
     uint64_t* st_free;     // [4]
@@ -101,7 +102,6 @@ __device__ __forceinline__ Bars bars_at(uint8_t* smem) {
     Bars r;
     r.q_full = b; b += 1;
     r.kv_full = b; b += kStages;
-    r.kv_empty = b; b += kStages;
     r.meta_full = b; b += kMetaSlots;
     r.meta_empty = b; b += kMetaSlots;
     r.s_full = b; b += 2;
@@ -139,7 +139,8 @@ __device__ void producer(const Params& p, uint8_t* smem, const Bars& B, volatile
     int loaded = 0;
     for (int j = 0; j < p.T; ++j) {
         const int s = j % kStages, u = j / kStages;
-        if (u > 0 && !mbar_wait(&B.kv_empty[s], (u - 1) & 1, abort)) break;
+        // stage s last held tile j - kStages, free once PV of that tile is done (o_full of its buffer)
+        if (u > 0 && !mbar_wait(&B.o_full[(j - kStages) & 1], ((j - kStages) >> 1) & 1, abort)) break;
         uint8_t* st = smem + kOffStages + s * kStageBytes;
         mbar_arrive_expect_tx(&B.kv_full[s], 2 * kTile);
         tma_load_3d(st, &p.tm_k, &B.kv_full[s], 0, j * kBN, head);
@@ -170,51 +171,80 @@ __device__ void meta_producer(const Params& p, uint8_t* smem, const Bars& B, vol
             drain_wait(&B.meta_full[s], ((loaded - 1 - s) / kMetaSlots) & 1);
 }
 
+// The MMA thread shares its SM sub-partition with four busy softmax /
+// correction warps, and every instruction it issues waits for a scheduler
+// slot (a microbenchmark: 64 cycles per MMA alone, ~270 next to four FMA-bound
+// warps).  So its instruction stream is kept short: shared-memory descriptors
+// differ only in the low word (start address >> 4), which the loop advances
+// by constants; the high word (stride, version, 128B swizzle) is one register.
+__device__ __forceinline__ void mma_ss_lo(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo, uint32_t hi, uint32_t idesc,
+                                          uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t.reg .b64 da, db;\n\t"
+        "mov.b64 da, {%1, %3};\n\t"
+        "mov.b64 db, {%2, %3};\n\t"
+        "setp.ne.b32 p, %5, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], da, db, %4, p;\n\t}"
+        ::"r"(d_tmem), "r"(a_lo), "r"(b_lo), "r"(hi), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void mma_ts_lo(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t hi, uint32_t idesc,
+                                          uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t.reg .b64 db;\n\t"
+        "mov.b64 db, {%2, %3};\n\t"
+        "setp.ne.b32 p, %5, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], [%1], db, %4, p;\n\t}"
+        ::"r"(d_tmem), "r"(a_tmem), "r"(b_lo), "r"(hi), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// The tile loop is unrolled by the 4 K/V stages, so stage and TMEM buffer
+// offsets are compile-time constants.
 __device__ void mma_issuer(const Params& p, uint8_t* smem, const Bars& B, volatile int* abort, uint32_t tmem) {
     const uint32_t idesc = idesc_e4m3_f32(kBM, kBN);
-    const uint64_t qdesc = smem_desc_k128(smem + kOffQ);
-    auto issue_qk = [&](int j) -> bool {
-        const int s = j % kStages;
-        if (!mbar_wait(&B.kv_full[s], (j / kStages) & 1, abort)) return false;
-        tc_fence_after();
-        const uint64_t kdesc = smem_desc_k128(smem + kOffStages + s * kStageBytes);
-        const uint32_t d = tmem + kColS + (j & 1) * kBN;
+    const uint64_t q64 = smem_desc_k128(smem + kOffQ);
+    const uint32_t hi = (uint32_t)(q64 >> 32);
+    const uint32_t qlo = (uint32_t)q64;
+    // descriptor low word of stage 0's K tile; the others are constant offsets (bytes >> 4)
+    const uint32_t k0lo = (uint32_t)smem_desc_k128(smem + kOffStages);
+    constexpr uint32_t kStageLo = kStageBytes >> 4, kTileLo = kTile >> 4;
+    auto qk = [&](uint32_t d, uint32_t klo) {
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) mma_f8_ss(d, qdesc + 2 * kk, kdesc + 2 * kk, idesc, kk > 0);
-        mma_commit(&B.s_full[j & 1]);
-        return true;
+        for (int kk = 0; kk < 4; ++kk) mma_ss_lo(d, qlo + 2 * kk, klo + 2 * kk, hi, idesc, kk > 0);
     };
     bool ok = mbar_wait(B.q_full, 0, abort);
-    if (ok && p.T > 0) ok = issue_qk(0);
-    if (ok && p.T > 1) ok = issue_qk(1);
-    for (int j = 0; ok && j < p.T; ++j) {
-        const int b = j & 1;
-        // P_j sits in S_j's TMEM columns (each softmax half over its own 64
-        // scores): keys 0-63 at columns 0-15, keys 64-127 at columns 64-79.
-        if (!mbar_wait(&B.p_full[b], (j >> 1) & 1, abort)) break;
-        if (j >= 2 && !mbar_wait(&B.o_free[b], ((j - 2) >> 1) & 1, abort)) break;
-        // K_{j+2} is waited for before PV_j, so that PV_j and QK_{j+2} reach
-        // the tensor pipe back to back
-        const int s2 = (j + 2) % kStages;
-        if (j + 2 < p.T && !mbar_wait(&B.kv_full[s2], ((j + 2) / kStages) & 1, abort)) break;
+    for (int j = 0; ok && j < 2 && j < p.T; ++j) {
+        if (!mbar_wait(&B.kv_full[j], 0, abort)) { ok = false; break; }
         tc_fence_after();
-        const int s = j % kStages;
-        const uint64_t vdesc = smem_desc_k128(smem + kOffStages + s * kStageBytes + kTile);
-        const uint32_t d = tmem + kColO + b * 128;
+        qk(tmem + kColS + j * kBN, k0lo + j * kStageLo);
+        mma_commit(&B.s_full[j]);
+    }
+    auto step = [&](auto U_, int j) -> bool {
+        constexpr int U = decltype(U_)::value;       // j % 4
+        constexpr int b = U & 1, s = U, s2 = (U + 2) & 3;
+        if (!mbar_wait(&B.p_full[b], (j >> 1) & 1, abort)) return false;
+        if (j >= 2 && !mbar_wait(&B.o_free[b], ((j - 2) >> 1) & 1, abort)) return false;
+        const bool next = j + 2 < p.T;
+        if (next && !mbar_wait(&B.kv_full[s2], ((j + 2) >> 2) & 1, abort)) return false;
+        tc_fence_after();
         const uint32_t pa = tmem + kColS + b * kBN;
+        const uint32_t vlo = k0lo + s * kStageLo + kTileLo;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
-            mma_f8_ts(d, pa + (kk >> 1) * 64 + (kk & 1) * 8, vdesc + 2 * kk, idesc, kk > 0);
-        mma_commit(&B.o_full[b]);
-        mma_commit(&B.kv_empty[s]);
-        // QK_{j+2} overwrites S_j / P_j: the tensor pipe runs in issue order,
-        // so it starts after PV_j has read P_j
-        if (j + 2 < p.T) {
-            const uint64_t kdesc = smem_desc_k128(smem + kOffStages + s2 * kStageBytes);
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk) mma_f8_ss(pa, qdesc + 2 * kk, kdesc + 2 * kk, idesc, kk > 0);
+            mma_ts_lo(tmem + kColO + b * 128, pa + (kk >> 1) * 64 + (kk & 1) * 8, vlo + 2 * kk, hi, idesc, kk > 0);
+        mma_commit(&B.o_full[b]);      // also frees K/V stage s (the producer waits on it)
+        if (next) {
+            qk(pa, k0lo + s2 * kStageLo);
             mma_commit(&B.s_full[b]);
         }
+        return true;
+    };
+    for (int j = 0; ok && j < p.T; j += 4) {
+        ok = step(std::integral_constant<int, 0>{}, j);
+        if (ok && j + 1 < p.T) ok = step(std::integral_constant<int, 1>{}, j + 1);
+        if (ok && j + 2 < p.T) ok = step(std::integral_constant<int, 2>{}, j + 2);
+        if (ok && j + 3 < p.T) ok = step(std::integral_constant<int, 3>{}, j + 3);
     }
     mma_commit(B.drain);
     drain_wait(B.drain, 0);
@@ -473,10 +503,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
 
     if (threadIdx.x == 0) {
         mbar_init(B.q_full, 1);
-        for (int s = 0; s < kStages; ++s) {
-            mbar_init(&B.kv_full[s], 1);
-            mbar_init(&B.kv_empty[s], 1);         // MMA commit after PV
-        }
+        for (int s = 0; s < kStages; ++s) mbar_init(&B.kv_full[s], 1);
         for (int s = 0; s < kMetaSlots; ++s) {
             mbar_init(&B.meta_full[s], 1);
             mbar_init(&B.meta_empty[s], 8);       // 8 correction warps
@@ -504,18 +531,18 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    // Register split of the 640 x 96 launch budget: producer/MMA group 32,
-    // softmax groups 96 (unchanged), correction groups 120; 4096 + 24576 +
-    // 30720 = 59392 <= 61440.
+    // Register split of the 640 x 96 launch budget: producer/MMA group 64
+    // (the unrolled MMA loop spills below that), softmax groups 96
+    // (unchanged), correction groups 112; 8192 + 24576 + 28672 = 61440.
     if (warp < 4) {
-        reg_dealloc<32>();
+        reg_dealloc<64>();
         if (warp == 0 && lane == 0) producer(p, smem, B, abort, qtile, head);
         if (warp == 1 && lane == 0) mma_issuer(p, smem, B, abort, tmem);
         if (warp == 2 && lane == 0) meta_producer(p, smem, B, abort, head);
     } else if (warp < 12) {
         softmax_role<EXPCAST>(p, smem, B, abort, tmem, qtile, head, warp & 3, (warp - 4) >> 2, lane);
     } else {
-        reg_alloc<120>();
+        reg_alloc<112>();
         correction_role<HAS_MEAN>(p, smem, B, abort, tmem, qtile, head, warp & 3, (warp - 12) >> 2, lane);
     }
     tc_fence_before();

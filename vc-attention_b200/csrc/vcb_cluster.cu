@@ -336,8 +336,8 @@ __global__ void __launch_bounds__(256, 2) cluster_assign128_kernel(ClusterArgs a
     if (tid < count) a.pcnt[((int64_t)h * a.nchunk + chunk) * count + tid] = cnt[tid];
 }
 
-// One CTA per (head, cluster), thread d per channel; chunks added in order.
-// The loads are independent (32 in flight per thread), only the adds chain.
+// One CTA per (head, cluster), thread d per channel; chunks added in order
+// (the loads are independent, only the adds are chained).
 __global__ void __launch_bounds__(128) cluster_update_kernel(ClusterArgs a) {
     const int64_t h = blockIdx.x;
     const int c = blockIdx.y, d = threadIdx.x;
@@ -347,20 +347,10 @@ __global__ void __launch_bounds__(128) cluster_update_kernel(ClusterArgs a) {
     const int64_t stride = (int64_t)a.count * 128;
     float total = 0.0f;
     long long n = 0;
-    for (int ch0 = 0; ch0 < a.nchunk; ch0 += 32) {
-        float x[32];
-        int k[32];
-#pragma unroll
-        for (int u = 0; u < 32; ++u) {
-            const bool in = ch0 + u < a.nchunk;
-            x[u] = in ? __ldg(src + (ch0 + u) * stride) : 0.0f;
-            k[u] = in ? __ldg(cnt + (int64_t)(ch0 + u) * a.count) : 0;
-        }
-#pragma unroll
-        for (int u = 0; u < 32; ++u) {
-            if (ch0 + u < a.nchunk) total += x[u];
-            n += k[u];
-        }
+#pragma unroll 8
+    for (int ch = 0; ch < a.nchunk; ++ch) {
+        total += __ldg(src + ch * stride);
+        n += __ldg(cnt + (int64_t)ch * a.count);
     }
     if (n > 0) a.centers[(h * a.count + c) * a.D + d] = total / (float)n;
 }

@@ -17,7 +17,9 @@
  *                      each lane sums its rows in increasing order, the chunk
  *                      sum adds lanes 0..LANES-1 in order, the head total adds
  *                      chunks in order, mean = total / S.
- *   V block mean     : per (tile, channel) tokens are added in tile order.
+ *   V block mean     : per (tile, channel) token j of the tile goes to
+ *                      partial sum j % 4 (each in tile order), then
+ *                      (p0 + p1) + (p2 + p3).
  *   Lloyd distances  : ||x||^2, ||c||^2 and x.c are fmaf chains over channels
  *                      0..D-1; distance = (xx + cc) - 2*xc, first minimum wins.
  *   Lloyd sums       : tokens are split into chunks of VCO_LLOYD_CHUNK and
@@ -326,13 +328,13 @@ void vco_value_tiles(const float* v, int64_t heads, int64_t S, int Dv, const int
                 int64_t meta = (h * T + t) * 128 + c;
                 uint8_t* out = payload + meta * kv_block;
                 if (c >= Dv) { vscale[meta] = 1.0f; mu[meta] = 0.0f; continue; }
-                float sum = 0.0f, mean = 0.0f;
+                float part[4] = {0.0f, 0.0f, 0.0f, 0.0f}, mean = 0.0f;
                 if (active) {
                     for (int j = 0; j < cnt; ++j) {
                         int64_t tok = pi ? pi[h * S + s0 + j] : s0 + j;
-                        sum += v[(h * S + tok) * Dv + c];
+                        part[j & 3] += v[(h * S + tok) * Dv + c];
                     }
-                    mean = sum / (float)cnt;
+                    mean = ((part[0] + part[1]) + (part[2] + part[3])) / (float)cnt;
                 }
                 float amax = 0.0f;
                 for (int j = 0; j < cnt; ++j) {

@@ -5,7 +5,8 @@
 //
 // One CTA per (head, 128-token tile): the tile's tokens are gathered through
 // the permutation with coalesced row loads into shared memory (fp32), then
-// thread c owns channel c: block mean (tokens added in tile order), residual,
+// thread c owns channel c: block mean (four interleaved partial sums in tile
+// order, see below), residual,
 // per-channel scale with the mean-dtype finite-storage guard, E4M3 residual
 // written channel-major (the K-major B operand of the PV MMA), and the
 // scaled mean rounded to the mean dtype.
@@ -87,14 +88,35 @@ __global__ void __launch_bounds__(128) vprep_kernel(const T* __restrict__ v, int
     uint32_t packed[32];
     float scale = 1.0f, stored = 0.0f;
     if (c < dv) {
-        float mean = 0.0f;
-        if (active) {
-            float sum = 0.0f;
-            for (int j = 0; j < cnt; ++j) sum += tile[j * 128 + c];
-            mean = sum / (float)cnt;
+        // One pass: the sum as four interleaved partial sums (token j into
+        // part j % 4, each in token order, then (p0 + p1) + (p2 + p3)), and
+        // the channel's min and max.  max |fl(x - mean)| is
+        // max(fl(xmax - mean), fl(mean - xmin)), since rounding is monotone
+        // and odd, so no second pass is needed for the scale.
+        float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        float xmax = -INFINITY, xmin = INFINITY;
+        if (cnt == kTile) {
+#pragma unroll 8
+            for (int j = 0; j < kTile; j += 4) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float x = tile[(j + e) * 128 + c];
+                    part[e] += x;
+                    xmax = fmaxf(xmax, x);
+                    xmin = fminf(xmin, x);
+                }
+            }
+        } else {
+            for (int j = 0; j < cnt; ++j) {
+                const float x = tile[j * 128 + c];
+                part[j & 3] += x;
+                xmax = fmaxf(xmax, x);
+                xmin = fminf(xmin, x);
+            }
         }
-        float amax = 0.0f;
-        for (int j = 0; j < cnt; ++j) amax = fmaxf(amax, fabsf(tile[j * 128 + c] - mean));
+        float mean = 0.0f;
+        if (active) mean = __fadd_rn(__fadd_rn(part[0], part[1]), __fadd_rn(part[2], part[3])) / (float)cnt;
+        const float amax = fmaxf(fmaxf(0.0f, __fsub_rn(xmax, mean)), __fsub_rn(mean, xmin));
         scale = amax / 448.0f;
         if (scale == 0.0f) scale = 1.0f;
         const float limit = mean_type == 1 ? 65504.0f : mean_type == 2 ? 3.3895313892515355e38f : 3.4028234663852886e38f;

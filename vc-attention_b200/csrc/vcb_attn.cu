@@ -123,6 +123,16 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
     }
 }
 
+// 2^x as the single MUFU.EX2 instruction, flushing subnormal results to zero.
+// The softmax's P = 2^g lies in [0, 256]; a result below 2^-126 encodes to
+// E4M3 zero either way and cannot move an FP32 row mass of at least 256, so
+// this gives the same bytes and mass as exp2f with fewer instructions.
+__device__ __forceinline__ float ex2_ftz(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 __device__ __forceinline__ uint32_t cvt_relu_f16x2(float hi, float lo) {
     uint32_t d;
     asm("cvt.rn.relu.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
@@ -363,7 +373,7 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, vola
                 add_f16x2_to_f32(ms[0], ms[1], h01 << 7);
                 add_f16x2_to_f32(ms[2], ms[3], h23 << 7);
             } else {
-                const float e0 = exp2f(g01.x), e1 = exp2f(g01.y), e2 = exp2f(g23.x), e3 = exp2f(g23.y);
+                const float e0 = ex2_ftz(g01.x), e1 = ex2_ftz(g01.y), e2 = ex2_ftz(g23.x), e3 = ex2_ftz(g23.y);
                 ms[0] = __fadd_rn(ms[0], e0);
                 ms[1] = __fadd_rn(ms[1], e1);
                 ms[2] = __fadd_rn(ms[2], e2);

@@ -374,10 +374,10 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, vola
                 add_f16x2_to_f32(ms[2], ms[3], h23 << 7);
             } else {
                 const float e0 = ex2_ftz(g01.x), e1 = ex2_ftz(g01.y), e2 = ex2_ftz(g23.x), e3 = ex2_ftz(g23.y);
-                ms[0] = __fadd_rn(ms[0], e0);
-                ms[1] = __fadd_rn(ms[1], e1);
-                ms[2] = __fadd_rn(ms[2], e2);
-                ms[3] = __fadd_rn(ms[3], e3);
+                // packed adds: each lane is the same round-to-nearest FP32 add
+                const float2 s01 = fadd2(make_float2(ms[0], ms[1]), make_float2(e0, e1));
+                const float2 s23 = fadd2(make_float2(ms[2], ms[3]), make_float2(e2, e3));
+                ms[0] = s01.x; ms[1] = s01.y; ms[2] = s23.x; ms[3] = s23.y;
                 pk[w] = e4m3x2(e0, e1) | (e4m3x2(e2, e3) << 16);
             }
         }

@@ -344,7 +344,10 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, vola
         const float rmax = fmaxf(pmax, omax);
         const float c = __fmul_rn(__fmul_rn(qs_scale, ks), p.scale);
         const float m_new = fmaxf(m, __fmul_rn(rmax, c));
-        const float alpha = expf(m - m_new);
+        // alpha = e^(m - m_new) as 2^((m - m_new) log2 e) on MUFU.EX2: a few
+        // FP32 ulps from expf, inside the output tolerance, and exactly 1
+        // when the maximum did not move (the correction skips its rescale then)
+        const float alpha = ex2_ftz(__fmul_rn(m - m_new, kLog2e));
         float A, Bc;
         if (EXPCAST) {
             A = __fmul_rn(c, kC1);

@@ -325,11 +325,13 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, vola
         tmem_ld16x2_at<0>(ts, r);
         tmem_ld16x2_at<32>(ts + 32, r);
         tmem_wait_ld();
-        const int nvalid = (int)min((int64_t)kBN, p.sk - (int64_t)j * kBN) - 64 * hs;
-        if (nvalid < 64) {
+        if (j == p.T - 1) {             // only the last tile can be partial
+            const int nvalid = (int)(p.sk - (int64_t)j * kBN) - 64 * hs;
+            if (nvalid < 64) {
 #pragma unroll
-            for (int i = 0; i < 64; ++i)
-                if (i >= nvalid) r[i] = 0xff800000u;   // -inf: masked key
+                for (int i = 0; i < 64; ++i)
+                    if (i >= nvalid) r[i] = 0xff800000u;   // -inf: masked key
+            }
         }
         float mx[4];
 #pragma unroll
@@ -350,12 +352,12 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, vola
         const float alpha = ex2_ftz(__fmul_rn(m - m_new, kLog2e));
         float A, Bc;
         if (EXPCAST) {
-            A = __fmul_rn(c, kC1);
-            Bc = __fsub_rn(kC2, __fmul_rn(m_new, kC1));
+            // in units of 2^-24 throughout: scaling by a power of two is exact,
+            // so this is the unscaled computation times 2^-24, bit for bit
+            A = __fmul_rn(c, kC1 * kTwoM24);
+            Bc = __fsub_rn(kC2 * kTwoM24, __fmul_rn(m_new, kC1 * kTwoM24));
             const float umax = fmaf(rmax, A, Bc);
-            if (umax > 120.25f) Bc = __fsub_rn(Bc, __fsub_rn(umax, kC2));
-            A = __fmul_rn(A, kTwoM24);
-            Bc = __fmul_rn(Bc, kTwoM24);
+            if (umax > 120.25f * kTwoM24) Bc = __fsub_rn(Bc, __fsub_rn(umax, kC2 * kTwoM24));
         } else {
             A = __fmul_rn(c, kLog2e);
             Bc = __fsub_rn(8.0f, __fmul_rn(m_new, kLog2e));

@@ -25,6 +25,13 @@ cpu_baseline / --impl reference
           cores, on a bounded sample (one head: all 256 query tiles over all
           keys for the baseline leg, 128 per step for --impl reference, with
           that head's full preprocessing), scaled to TFLOPS.
+
+Other cases (not the bench line):
+    --case attn|prep --heads H    small single-GPU cases for ncu
+    --case ulysses                configuration 4 sequence-sharded (torchrun)
+    --case schedule [--heads H --seq S]
+                                  configuration 5's 50-step denoising loop in
+                                  every mode, step times per schedule phase
 """
 from __future__ import annotations
 
@@ -401,6 +408,46 @@ def run_case(args):
                       "tflops": [flops(h=args.heads) / (t * 1e-3) / 1e12 for t in times]}))
 
 
+def run_schedule(args):
+    """Config 5's denoising loop on one GPU: 50 steps with fresh seeded Q/K/V per step
+    (centres drifting), every mode, one LayoutCache per mode and layer.  With 50 steps the
+    smoothing window is steps 0-12 and the layout is refreshed at steps 0, 4, 8 and 12
+    (core.py:182-211).  Reports the mean step time per phase (refresh / smoothed with the
+    cached layout / unsmoothed) and over the whole loop, CUDA events around each call."""
+    from vc_attention_b200 import Config, LayoutCache, attention
+    from vc_attention_b200.synthetic import make_qkv
+
+    heads, seq, total = args.heads, args.seq, 50
+    arms = {"fp8_control": (False, False), "expcast": (False, True), "v_smooth": (True, False),
+            "combined": (True, True)}
+    out = {"case": "schedule", "workload": f"c5 generator: B1 H{heads} S{seq} D128 bf16, {total} steps",
+           "modes": {}}
+    for mode, (smooth, cast) in arms.items():
+        cfg = Config(v_smooth=smooth, expcast=cast)
+        cache = LayoutCache(cfg)
+        phases = {"refresh": [], "smoothed_cached": [], "unsmoothed": []}
+        for step in range(total):
+            q, k, v = make_qkv("c5", 11, device="cuda", heads=heads, seq=seq, step=step)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            _, stats = attention(q, k, v, cfg, cache=cache, step=step, total_steps=total, request_id=mode,
+                                 layer_id=0)
+            e.record()
+            e.synchronize()
+            phase = ("refresh" if stats["layout_refreshed"] else
+                     "smoothed_cached" if stats["smoothing_active"] else "unsmoothed")
+            phases[phase].append(s.elapsed_time(e))
+        mean = {k: (sum(v) / len(v) if v else None) for k, v in phases.items()}
+        steps_ms = [t for v in phases.values() for t in v]
+        out["modes"][mode] = {
+            "steps": {k: len(v) for k, v in phases.items()},
+            "ms": mean,
+            "mean_ms": sum(steps_ms) / len(steps_ms),
+            "tflops_mean": 4.0 * heads * seq * seq * 128 / (sum(steps_ms) / len(steps_ms) * 1e-3) / 1e12,
+        }
+    print(json.dumps(out))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -408,12 +455,17 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--case", choices=("attn", "prep", "ulysses"),
-                    help="attn / prep: small single-GPU cases for profilers; ulysses: config 4 sequence-sharded")
+    ap.add_argument("--case", choices=("attn", "prep", "ulysses", "schedule"),
+                    help="attn / prep: small single-GPU cases for profilers; ulysses: config 4 "
+                         "sequence-sharded; schedule: config 5's 50-step loop in every mode")
     ap.add_argument("--heads", type=int, default=16, help="heads of the --case run")
+    ap.add_argument("--seq", type=int, default=65536, help="sequence length of --case schedule")
     args = ap.parse_args()
     if args.case in ("attn", "prep"):
         run_case(args)
+        return
+    if args.case == "schedule":
+        run_schedule(args)
         return
     world, rank, local = dist_setup()
     try:

@@ -180,8 +180,11 @@ __global__ void __launch_bounds__(256) cluster_assign_kernel(ClusterArgs a) {
 // D == 128: the chunk's rows are staged in shared memory once (coalesced
 // 16-byte loads, 16-byte chunks XOR-swizzled by row so that a warp reading
 // one chunk of 32 rows hits every bank group), then
-//   distances  thread t = token t, channels streamed in order from shared
-//              memory (same fmaf chains as above);
+//   distances  thread t = tokens t % 128 and t % 128 + 128 in the two lanes
+//              of packed FMAs against a doubled centre table, half of the
+//              clusters per thread (t / 128); channels streamed in order from
+//              shared memory, so every (token, cluster) chain is the fmaf
+//              chain above; the two halves' first minima are merged;
 //   sums       warp w = sub-chunk w (tokens 32w..32w+31), lane = 4 channels,
 //              the token loop in order with a warp-uniform switch on the
 //              label; sub-chunk sums added in order by thread (cluster, d).
@@ -193,8 +196,11 @@ __global__ void __launch_bounds__(256, 2) cluster_assign128_kernel(ClusterArgs a
     extern __shared__ __align__(16) uint8_t dsm[];
     uint8_t* xs = dsm;                                               // [256][RB], swizzled
     float* subs = reinterpret_cast<float*>(dsm + kChunk * RB);        // [8 warps][8 clusters][128]
-    __shared__ __align__(16) float cen[kMaxClusters * 128];   // [c / 8][d][c % 8]
+    // centres twice over for packed FMAs over two tokens: [c / 4][d][c % 4][2]
+    float* cen2 = subs + 8 * 8 * 128;
     __shared__ float cnorm[kMaxClusters];
+    __shared__ float hbest[2][kChunk];
+    __shared__ uint8_t hidx[2][kChunk];
     __shared__ uint8_t lab[kChunk];
     __shared__ int cnt[kMaxClusters];
     const int64_t h = blockIdx.y;
@@ -203,9 +209,11 @@ __global__ void __launch_bounds__(256, 2) cluster_assign128_kernel(ClusterArgs a
     const int count = a.count;
     const int64_t base = (int64_t)chunk * kChunk;
     const int nvalid = (int)min((int64_t)kChunk, a.S - base);
-    for (int i = tid; i < kMaxClusters * 128; i += 256) {
+    const int ngroups = (count + 3) >> 2;
+    for (int i = tid; i < ngroups * 4 * 128; i += 256) {
         const int c = i / 128, d = i % 128;
-        cen[(c >> 3) * 1024 + d * 8 + (c & 7)] = c < count ? a.centers[(h * count) * 128 + i] : 0.0f;
+        const float val = c < count ? a.centers[(h * count) * 128 + i] : 0.0f;
+        *reinterpret_cast<float2*>(cen2 + ((c >> 2) * 128 + d) * 8 + (c & 3) * 2) = make_float2(val, val);
     }
     if (tid < kMaxClusters) cnt[tid] = 0;
     const uint4* src = reinterpret_cast<const uint4*>(static_cast<const T*>(a.v) + (h * a.S + base) * 128);
@@ -230,59 +238,82 @@ __global__ void __launch_bounds__(256, 2) cluster_assign128_kernel(ClusterArgs a
     __syncthreads();
     if (tid < count) {
         float acc = 0.0f;
-        const float* ct = cen + (tid >> 3) * 1024 + (tid & 7);
+        const float* ct = cen2 + (tid >> 2) * 1024 + (tid & 3) * 2;
         for (int d = 0; d < 128; ++d) acc = fmaf(ct[d * 8], ct[d * 8], acc);
         cnorm[tid] = acc;
     }
     __syncthreads();
 
-    if (tid < nvalid) {
-        const uint8_t* xr = xs + tid * RB;
-        const int sw = tid & (NCH - 1);
-        float xx = 0.0f, bestd = 0.0f;
-        int best = 0;
-        for (int c0 = 0; c0 < count; c0 += 8) {
-            // two clusters per packed FMA: acc2[p] holds clusters c0 + 2p, c0 + 2p + 1;
-            // each cluster's chain still runs over d = 0..127 in order
-            const float* cg = cen + (c0 >> 3) * 1024;
-            float2 acc2[4];
+    {
+        // thread t: tokens p and p + 128 (p = t % 128) in the two lanes of each
+        // packed FMA, clusters 4 * (2g + half) .. + 3 of every group of eight
+        // (half = t / 128); each (token, cluster) chain still runs over
+        // d = 0..127 in order, as in the scalar form
+        const int p = tid & 127, half = tid >> 7;
+        const uint8_t* xa = xs + p * RB;
+        const uint8_t* xb = xs + (p + 128) * RB;
+        const int sw = p & (NCH - 1);            // (p + 128) & (NCH - 1) is the same
+        float2 xx = make_float2(0.0f, 0.0f);
+        float bd[2] = {0.0f, 0.0f};
+        int bi[2] = {-1, -1};
+        for (int c0 = 4 * half; c0 < count; c0 += 8) {
+            const float* cg = cen2 + (c0 >> 2) * 1024;
+            float2 acc[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) acc2[i] = make_float2(0.0f, 0.0f);
+            for (int i = 0; i < 4; ++i) acc[i] = make_float2(0.0f, 0.0f);
 #pragma unroll 2
             for (int k = 0; k < NCH; ++k) {
-                const uint4 raw = *reinterpret_cast<const uint4*>(xr + ((k ^ sw) << 4));
-                float x[E];
+                const uint4 ra = *reinterpret_cast<const uint4*>(xa + ((k ^ sw) << 4));
+                const uint4 rb = *reinterpret_cast<const uint4*>(xb + ((k ^ sw) << 4));
+                float x0[E], x1[E];
                 if constexpr (sizeof(T) == 4) {
-                    x[0] = __uint_as_float(raw.x); x[1] = __uint_as_float(raw.y);
-                    x[2] = __uint_as_float(raw.z); x[3] = __uint_as_float(raw.w);
+                    x0[0] = __uint_as_float(ra.x); x0[1] = __uint_as_float(ra.y);
+                    x0[2] = __uint_as_float(ra.z); x0[3] = __uint_as_float(ra.w);
+                    x1[0] = __uint_as_float(rb.x); x1[1] = __uint_as_float(rb.y);
+                    x1[2] = __uint_as_float(rb.z); x1[3] = __uint_as_float(rb.w);
                 } else {
-                    const T* hv = reinterpret_cast<const T*>(&raw);
+                    const T* ha = reinterpret_cast<const T*>(&ra);
+                    const T* hb = reinterpret_cast<const T*>(&rb);
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) x[e] = to_float(hv[e]);
+                    for (int e = 0; e < 8; ++e) { x0[e] = to_float(ha[e]); x1[e] = to_float(hb[e]); }
                 }
 #pragma unroll
                 for (int e = 0; e < E; ++e) {
                     const int d = k * E + e;
-                    if (c0 == 0) xx = fmaf(x[e], x[e], xx);
+                    const float2 x2 = make_float2(x0[e], x1[e]);
+                    if (c0 < 8) xx = ffma2(x2, x2, xx);
                     const float4 ca = *reinterpret_cast<const float4*>(cg + d * 8);
                     const float4 cb = *reinterpret_cast<const float4*>(cg + d * 8 + 4);
-                    const float2 x2 = make_float2(x[e], x[e]);
-                    acc2[0] = ffma2(x2, make_float2(ca.x, ca.y), acc2[0]);
-                    acc2[1] = ffma2(x2, make_float2(ca.z, ca.w), acc2[1]);
-                    acc2[2] = ffma2(x2, make_float2(cb.x, cb.y), acc2[2]);
-                    acc2[3] = ffma2(x2, make_float2(cb.z, cb.w), acc2[3]);
+                    acc[0] = ffma2(x2, make_float2(ca.x, ca.y), acc[0]);
+                    acc[1] = ffma2(x2, make_float2(ca.z, ca.w), acc[1]);
+                    acc[2] = ffma2(x2, make_float2(cb.x, cb.y), acc[2]);
+                    acc[3] = ffma2(x2, make_float2(cb.z, cb.w), acc[3]);
                 }
             }
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
+            for (int i = 0; i < 4; ++i) {
                 const int c = c0 + i;
                 if (c < count) {
-                    const float dot = (i & 1) ? acc2[i >> 1].y : acc2[i >> 1].x;
-                    const float dist = __fsub_rn(__fadd_rn(xx, cnorm[c]), __fmul_rn(2.0f, dot));
-                    if (c == 0 || dist < bestd) { bestd = dist; best = c; }
+                    const float cn = cnorm[c];
+                    const float d0 = __fsub_rn(__fadd_rn(xx.x, cn), __fmul_rn(2.0f, acc[i].x));
+                    const float d1 = __fsub_rn(__fadd_rn(xx.y, cn), __fmul_rn(2.0f, acc[i].y));
+                    if (bi[0] < 0 || d0 < bd[0]) { bd[0] = d0; bi[0] = c; }
+                    if (bi[1] < 0 || d1 < bd[1]) { bd[1] = d1; bi[1] = c; }
                 }
             }
         }
+        hbest[half][p] = bd[0]; hidx[half][p] = (uint8_t)(bi[0] < 0 ? 255 : bi[0]);
+        hbest[half][p + 128] = bd[1]; hidx[half][p + 128] = (uint8_t)(bi[1] < 0 ? 255 : bi[1]);
+    }
+    __syncthreads();
+    if (tid < nvalid) {
+        // the first minimum over all clusters: the smaller distance, and the
+        // smaller index on a tie (a half with no cluster has index 255)
+        int best = hidx[0][tid];
+        const int other = hidx[1][tid];
+        if (other != 255 && (best == 255 || hbest[1][tid] < hbest[0][tid] ||
+                             (hbest[1][tid] == hbest[0][tid] && other < best)))
+            best = other;
         lab[tid] = (uint8_t)best;
         a.labels[h * a.S + base + tid] = (uint8_t)best;
         atomicAdd(&cnt[best], 1);
@@ -444,7 +475,8 @@ int run(const vcb_group_args* p, cudaStream_t st) {
     linspace_indices(p->s, count, init.idx);
     cluster_init_kernel<T><<<(unsigned)p->heads, 256, 0, st>>>(a, p->centers_in, init);
     VCB_CUDA(cudaGetLastError());
-    const size_t fast_smem = (size_t)kChunk * 128 * sizeof(T) + 8 * 8 * 128 * sizeof(float);
+    const size_t fast_smem = (size_t)kChunk * 128 * sizeof(T) + 8 * 8 * 128 * sizeof(float) +
+                             (size_t)((count + 3) / 4) * 128 * 8 * sizeof(float);
     if (p->d == 128)
         VCB_CUDA(cudaFuncSetAttribute(cluster_assign128_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       (int)fast_smem));

@@ -67,11 +67,13 @@ __device__ __forceinline__ void load8(const __nv_bfloat16* p, float* o) {
 __device__ __forceinline__ bool finite_f(float x) { return fabsf(x) <= 3.402823466e38f; }
 
 // E4M3 (RNE, satfinite) of two fp32 values; lo goes to the low byte.
+// Two floats to E4M3 with round-to-nearest-even and saturation to +-448:
+// for finite input this is the reference's clamp to [-448, 448] followed by
+// the cast (core.py:121), without a separate clamp.
 __device__ __forceinline__ uint32_t e4m3x2(float lo, float hi) {
     return (uint32_t)__nv_cvt_float2_to_fp8x2(make_float2(lo, hi), __NV_SATFINITE, __NV_E4M3);
 }
 
-__device__ __forceinline__ float clamp448(float x) { return fminf(448.0f, fmaxf(-448.0f, x)); }
 
 // Correctly rounded x / b from y = RN(1/b) (Markstein 1990): q = RN(x y),
 // r = x - b q is exact with one FMA, RN(q + r y) is the IEEE quotient while

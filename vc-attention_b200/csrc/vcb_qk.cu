@@ -193,7 +193,7 @@ __device__ __forceinline__ bool transform_half(const RowArgs& a, int64_t h, int6
 }
 
 // 64 E4M3 bytes of a half row: x / scale as div_by(x * pre, bdiv, rdiv)
-// (the correctly rounded quotient), clamped to +-448.
+// (the correctly rounded quotient), saturated to +-448 by the E4M3 cast.
 __device__ __forceinline__ void encode_half(const float (&x)[64], int c0, int W, float pre, float bdiv,
                                             float rdiv, uint4* dst) {
 #pragma unroll
@@ -205,7 +205,7 @@ __device__ __forceinline__ void encode_half(const float (&x)[64], int c0, int W,
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
                 const int c = 16 * q + 4 * k + e;
-                v[e] = c0 + c < W ? clamp448(div_by(__fmul_rn(x[c], pre), bdiv, rdiv)) : 0.0f;
+                v[e] = c0 + c < W ? div_by(__fmul_rn(x[c], pre), bdiv, rdiv) : 0.0f;
             }
             w[k] = e4m3x2(v[0], v[1]) | (e4m3x2(v[2], v[3]) << 16);
         }

@@ -131,7 +131,7 @@ __global__ void __launch_bounds__(128) vprep_kernel(const T* __restrict__ v, int
             for (int e = 0; e < 4; ++e) {
                 const int j = 4 * w + e;
                 const float r = tile[j * 128 + c] - mean;
-                q[e] = j < cnt ? clamp448(div_by(__fmul_rn(r, pre), bdiv, rdiv)) : 0.0f;
+                q[e] = j < cnt ? div_by(__fmul_rn(r, pre), bdiv, rdiv) : 0.0f;
             }
             packed[w] = e4m3x2(q[0], q[1]) | (e4m3x2(q[2], q[3]) << 16);
         }

@@ -351,12 +351,21 @@ def test_nonfinite_input_is_rejected_and_cache_untouched():
     attention(q, k, v, cfg, cache=cache, step=0, total_steps=20, request_id="a")
     before = cache._states[0]
     for bad in ("q", "k", "v"):
-        t = {"q": q, "k": k, "v": v}
-        t[bad] = t[bad].clone()
-        t[bad][0, 0, 5, 3] = float("nan")
+        n, d = {"q": q, "k": k, "v": v}[bad].shape[2:]
+        for value, where in ((float("nan"), (0, 0, 5, 3)), (float("inf"), (0, 0, n - 1, d - 1)),
+                             (float("-inf"), (0, 0, n // 2, 0))):
+            t = {"q": q, "k": k, "v": v}
+            t[bad] = t[bad].clone()
+            t[bad][where] = value
+            with pytest.raises(ValueError, match="finite"):
+                attention(t["q"], t["k"], t["v"], cfg, cache=cache, step=4, total_steps=20, request_id="a")
+            assert cache._states[0] is before and cache._states[0]["step"] == 0
+    # past the smoothing window (no V mean) the check still covers V
+    for value in (float("nan"), float("inf")):
+        tv = v.clone()
+        tv[0, 0, 17, 9] = value
         with pytest.raises(ValueError, match="finite"):
-            attention(t["q"], t["k"], t["v"], cfg, cache=cache, step=4, total_steps=20, request_id="a")
-        assert cache._states[0] is before and cache._states[0]["step"] == 0
+            attention(q, k, tv, cfg, cache=LayoutCache(cfg), step=19, total_steps=20, request_id="b")
 
 
 @pytest.mark.parametrize("k_smooth,rotate", [(False, False), (False, True), (True, False), (True, True)])

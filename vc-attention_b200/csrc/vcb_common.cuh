@@ -66,6 +66,14 @@ __device__ __forceinline__ void load8(const __nv_bfloat16* p, float* o) {
 
 __device__ __forceinline__ bool finite_f(float x) { return fabsf(x) <= 3.402823466e38f; }
 
+// max that returns NaN when either input is NaN (max.NaN), so a block's amax
+// also tells whether every input was finite.
+__device__ __forceinline__ float fmax_nan(float a, float b) {
+    float d;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+    return d;
+}
+
 // E4M3 (RNE, satfinite) of two fp32 values; lo goes to the low byte.
 // Two floats to E4M3 with round-to-nearest-even and saturation to +-448:
 // for finite input this is the reference's clamp to [-448, 448] followed by

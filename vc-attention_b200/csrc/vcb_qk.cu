@@ -134,9 +134,8 @@ __device__ __forceinline__ bool transform_row(const RowArgs& a, int64_t h, int64
 // (left + right, left - right) on the same operands.
 // FIX: D == 128 with the 128-point Hadamard, every bound known at compile time.
 template <typename T, bool FIX>
-__device__ __forceinline__ bool transform_half(const RowArgs& a, int64_t h, int64_t r, bool valid, int half,
+__device__ __forceinline__ void transform_half(const RowArgs& a, int64_t h, int64_t r, bool valid, int half,
                                                const float* smean, float (&x)[64], int64_t tok_hint = -1) {
-    bool ok = true;
     const int c0 = 64 * half;
     const int D = FIX ? 128 : a.D;
     const int width = FIX ? 128 : a.width;
@@ -151,8 +150,6 @@ __device__ __forceinline__ bool transform_half(const RowArgs& a, int64_t h, int6
 #pragma unroll
             for (int c = 0; c < 64; ++c) x[c] = c0 + c < D ? Elem<T>::load(src + c0 + c) : 0.0f;
         }
-#pragma unroll
-        for (int c = 0; c < 64; ++c) ok &= finite_f(x[c]);
         if (smean) {
 #pragma unroll
             for (int c = 0; c < 64; ++c)
@@ -189,7 +186,6 @@ __device__ __forceinline__ bool transform_half(const RowArgs& a, int64_t h, int6
         for (int c = 0; c < 64; ++c)
             if (c0 + c < width) x[c] = x[c] * norm;
     }
-    return ok;
 }
 
 // 64 E4M3 bytes of a half row: x / scale as div_by(x * pre, bdiv, rdiv)
@@ -239,25 +235,27 @@ __global__ void __launch_bounds__(512) qk_quant_kernel(RowArgs a) {
     const int half = lane >> 4;
     const int rows_per_pass = nthr / 2;
     float x[64];
+    // max.NaN keeps a NaN (from a NaN or infinite input, or Inf - Inf in the
+    // transform) all the way to the block maximum, which is then the
+    // finiteness check of every input row of the block
     float amax = 0.0f;
-    bool ok = true;
     for (int base = 0; base < a.block; base += rows_per_pass) {
         const int rl = base + warp * 16 + (lane & 15);
         const int64_t r = r0 + rl;
         const bool valid = rl < a.block && r < a.S;
         const int64_t tok = single ? (a.pi ? (valid ? (int64_t)stok[rl] : 0) : r) : -1;
-        ok &= transform_half<T, FIX>(a, h, r, valid, half, sm, x, tok);
+        transform_half<T, FIX>(a, h, r, valid, half, sm, x, tok);
 #pragma unroll
         for (int c = 0; c < 64; ++c)
-            if (64 * half + c < W) amax = fmaxf(amax, fabsf(x[c]));
+            if (64 * half + c < W) amax = fmax_nan(amax, fabsf(x[c]));
     }
-    if (!ok) flag_status(a.status, VCB_FLAG_NONFINITE);
-    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    for (int o = 16; o > 0; o >>= 1) amax = fmax_nan(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     if (lane == 0) red[warp] = amax;
     __syncthreads();
     if (threadIdx.x == 0) {
         float bmax = 0.0f;
-        for (int w = 0; w < nthr / 32; ++w) bmax = fmaxf(bmax, red[w]);
+        for (int w = 0; w < nthr / 32; ++w) bmax = fmax_nan(bmax, red[w]);
+        if (!finite_f(bmax)) flag_status(a.status, VCB_FLAG_NONFINITE);
         float scale = bmax / 448.0f;
         if (scale == 0.0f) scale = 1.0f;
         if (b < a.nblk) a.scales[h * a.nblk + b] = scale;

@@ -190,6 +190,9 @@ __device__ __forceinline__ void transform_half(const RowArgs& a, int64_t h, int6
 
 // 64 E4M3 bytes of a half row: x / scale as div_by(x * pre, bdiv, rdiv)
 // (the correctly rounded quotient), saturated to +-448 by the E4M3 cast.
+// PRE: the scale was prescaled (tiny scales); otherwise pre == 1 and the
+// multiply by it is skipped, which changes nothing.
+template <bool PRE>
 __device__ __forceinline__ void encode_half(const float (&x)[64], int c0, int W, float pre, float bdiv,
                                             float rdiv, uint4* dst) {
 #pragma unroll
@@ -201,7 +204,7 @@ __device__ __forceinline__ void encode_half(const float (&x)[64], int c0, int W,
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
                 const int c = 16 * q + 4 * k + e;
-                v[e] = c0 + c < W ? div_by(__fmul_rn(x[c], pre), bdiv, rdiv) : 0.0f;
+                v[e] = c0 + c < W ? div_by(PRE ? __fmul_rn(x[c], pre) : x[c], bdiv, rdiv) : 0.0f;
             }
             w[k] = e4m3x2(v[0], v[1]) | (e4m3x2(v[2], v[3]) << 16);
         }
@@ -278,7 +281,8 @@ __global__ void __launch_bounds__(512) qk_quant_kernel(RowArgs a) {
             for (int q = 0; q < 4; ++q) dst[q] = make_uint4(0u, 0u, 0u, 0u);
             continue;
         }
-        encode_half(x, 64 * half, W, pre, bdiv, rdiv, dst);
+        if (pre == 1.0f) encode_half<false>(x, 64 * half, W, pre, bdiv, rdiv, dst);   // block-uniform
+        else encode_half<true>(x, 64 * half, W, pre, bdiv, rdiv, dst);
     }
 }
 

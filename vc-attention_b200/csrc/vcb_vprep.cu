@@ -4,12 +4,13 @@
 // gathered V in PyTorch, cuda_backend.py:51).
 //
 // One CTA per (head, 128-token tile): the tile's tokens are gathered through
-// the permutation with coalesced row loads into shared memory (fp32), then
-// thread c owns channel c: block mean (four interleaved partial sums in tile
-// order, see below), residual,
-// per-channel scale with the mean-dtype finite-storage guard, E4M3 residual
-// written channel-major (the K-major B operand of the PV MMA), and the
-// scaled mean rounded to the mean dtype.
+// the permutation with coalesced row loads into shared memory (staged in the
+// input type: 32 KB for bf16 / fp16, so more CTAs fit per SM), then
+// thread c owns channel c: the finiteness check, the block mean (four
+// interleaved partial sums in tile order, see below), residual, per-channel
+// scale with the mean-dtype finite-storage guard, E4M3 residual written
+// channel-major (the K-major B operand of the PV MMA), and the scaled mean
+// rounded to the mean dtype.
 #include "vcb_internal.h"
 
 namespace vcb {
@@ -25,7 +26,8 @@ __global__ void __launch_bounds__(128) vprep_kernel(const T* __restrict__ v, int
                                                     const int32_t* __restrict__ pi, int active,
                                                     int mean_type, int T_tiles, uint8_t* __restrict__ v8,
                                                     float* __restrict__ meta, int32_t* status) {
-    extern __shared__ float tile[];          // [kTile][128]
+    extern __shared__ __align__(16) uint8_t tile_raw[];
+    T* tile = reinterpret_cast<T*>(tile_raw);     // [kTile][128] in the input type
     const int64_t h = blockIdx.y;
     const int t = blockIdx.x;
     const int64_t s0 = (int64_t)t * kTile;
@@ -53,35 +55,18 @@ __global__ void __launch_bounds__(128) vprep_kernel(const T* __restrict__ v, int
 #pragma unroll
             for (int u = 0; u < kRound; ++u) {
                 const int g = threadIdx.x + 128 * (u0 + u), j = g / NP, k = g % NP;
-                float e[E];
-                const T* hv = reinterpret_cast<const T*>(&buf[u]);
-#pragma unroll
-                for (int i = 0; i < E; ++i) {
-                    e[i] = to_float(hv[i]);
-                    ok &= finite_f(e[i]);
-                }
-                float4* dst = reinterpret_cast<float4*>(tile + j * 128 + k * E);
-#pragma unroll
-                for (int i = 0; i < E / 4; ++i) dst[i] = make_float4(e[4 * i], e[4 * i + 1], e[4 * i + 2], e[4 * i + 3]);
+                *reinterpret_cast<uint4*>(tile + j * 128 + k * E) = buf[u];
             }
         }
     } else
     for (int j = warp; j < kTile; j += 4) {
-        float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (j < cnt) {
-            const T* row = v + (h * S + toks[j]) * dv;
-            float e[4];
+        const T* row = v + (h * S + toks[j < cnt ? j : 0]) * dv;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int c = 4 * lane + i;
-                e[i] = c < dv ? Elem<T>::load(row + c) : 0.0f;
-                ok &= finite_f(e[i]);
-            }
-            f = make_float4(e[0], e[1], e[2], e[3]);
+        for (int i = 0; i < 4; ++i) {
+            const int c = 4 * lane + i;
+            tile[j * 128 + c] = j < cnt && c < dv ? row[c] : T(0.0f);
         }
-        reinterpret_cast<float4*>(tile + j * 128)[lane] = f;
     }
-    if (!ok) flag_status(status, VCB_FLAG_NONFINITE);
     __syncthreads();
     const int c = threadIdx.x;
     const int64_t m = ((int64_t)h * T_tiles + t);
@@ -100,7 +85,8 @@ __global__ void __launch_bounds__(128) vprep_kernel(const T* __restrict__ v, int
             for (int j = 0; j < kTile; j += 4) {
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
-                    const float x = tile[(j + e) * 128 + c];
+                    const float x = to_float(tile[(j + e) * 128 + c]);
+                    ok &= finite_f(x);
                     part[e] += x;
                     xmax = fmaxf(xmax, x);
                     xmin = fminf(xmin, x);
@@ -108,7 +94,8 @@ __global__ void __launch_bounds__(128) vprep_kernel(const T* __restrict__ v, int
             }
         } else {
             for (int j = 0; j < cnt; ++j) {
-                const float x = tile[j * 128 + c];
+                const float x = to_float(tile[j * 128 + c]);
+                ok &= finite_f(x);
                 part[j & 3] += x;
                 xmax = fmaxf(xmax, x);
                 xmin = fminf(xmin, x);
@@ -116,6 +103,7 @@ __global__ void __launch_bounds__(128) vprep_kernel(const T* __restrict__ v, int
         }
         float mean = 0.0f;
         if (active) mean = __fadd_rn(__fadd_rn(part[0], part[1]), __fadd_rn(part[2], part[3])) / (float)cnt;
+        if (!ok) flag_status(status, VCB_FLAG_NONFINITE);
         const float amax = fmaxf(fmaxf(0.0f, __fsub_rn(xmax, mean)), __fsub_rn(mean, xmin));
         scale = amax / 448.0f;
         if (scale == 0.0f) scale = 1.0f;
@@ -130,7 +118,7 @@ __global__ void __launch_bounds__(128) vprep_kernel(const T* __restrict__ v, int
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
                 const int j = 4 * w + e;
-                const float r = tile[j * 128 + c] - mean;
+                const float r = to_float(tile[j * 128 + c]) - mean;
                 q[e] = j < cnt ? div_by(__fmul_rn(r, pre), bdiv, rdiv) : 0.0f;
             }
             packed[w] = e4m3x2(q[0], q[1]) | (e4m3x2(q[2], q[3]) << 16);
@@ -154,7 +142,7 @@ namespace {
 template <typename T>
 int launch(const vcb_v_args* p, cudaStream_t st) {
     const int T_tiles = (int)((p->s + kTile - 1) / kTile);
-    const size_t smem = kTile * 128 * sizeof(float);
+    const size_t smem = kTile * 128 * sizeof(T);
     VCB_CUDA(cudaFuncSetAttribute(vprep_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     vprep_kernel<T><<<dim3(T_tiles, (unsigned)p->heads), 128, smem, st>>>(
         static_cast<const T*>(p->v), p->s, p->dv, p->pi, p->active, p->mean_type, T_tiles, p->v8,

@@ -308,6 +308,8 @@ def run_ours(args, world, rank, local):
                            parallelism=f"{world} rank(s), {h_loc} heads each (contiguous head ranges), "
                                        "no collective"),
             "e2e": {"value": flops() / (e2e * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": e2e,
+                    "ms_per_step_median": statistics.median(e2e_ms),
+                    "steps_ms": [round(t, 3) for t in e2e_ms],
                     "h2d_bytes_per_step": 3 * nbytes, "d2h_bytes_per_step": nbytes},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": traffic, "kernel": "attn_kernel",

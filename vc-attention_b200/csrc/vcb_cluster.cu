@@ -185,9 +185,10 @@ __global__ void __launch_bounds__(256) cluster_assign_kernel(ClusterArgs a) {
 //              clusters per thread (t / 128); channels streamed in order from
 //              shared memory, so every (token, cluster) chain is the fmaf
 //              chain above; the two halves' first minima are merged;
-//   sums       warp w = sub-chunk w (tokens 32w..32w+31), lane = 4 channels,
-//              the token loop in order with a warp-uniform switch on the
-//              label; sub-chunk sums added in order by thread (cluster, d).
+//   sums       warp w = sub-chunk w (tokens 32w..32w+31), lane = 4 channels;
+//              per cluster, a ballot of the sub-chunk's labels gives that
+//              cluster's tokens, added lowest first (token order); sub-chunk
+//              sums added in order by thread (cluster, d).
 template <typename T>
 __global__ void __launch_bounds__(256, 2) cluster_assign128_kernel(ClusterArgs a) {
     constexpr int RB = 128 * (int)sizeof(T);        // bytes per staged row
@@ -328,25 +329,29 @@ __global__ void __launch_bounds__(256, 2) cluster_assign128_kernel(ClusterArgs a
         for (int i = 0; i < 8; ++i)
 #pragma unroll
             for (int e = 0; e < 4; ++e) s[i][e] = 0.0f;
-        for (int t = t0; t < t1; ++t) {
-            const int c = lab[t] - cg;
-            if (c < 0 || c >= 8) continue;              // warp-uniform
-            float x[4];
-            const uint8_t* xr = xs + t * RB;
-            if constexpr (sizeof(T) == 4) {
-                const float4 v = *reinterpret_cast<const float4*>(xr + ((lane ^ (t & (NCH - 1))) << 4));
-                x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
-            } else {
-                const uint2 raw = *reinterpret_cast<const uint2*>(xr + (((lane >> 1) ^ (t & (NCH - 1))) << 4) +
-                                                                  (lane & 1) * 8);
-                const T* hv = reinterpret_cast<const T*>(&raw);
+        // each cluster of the group takes its tokens of the sub-chunk in token
+        // order (lowest set bit first), the order of the per-token loop
+        const int mine = t0 + lane < t1 ? lab[t0 + lane] - cg : -1;
 #pragma unroll
-                for (int e = 0; e < 4; ++e) x[e] = to_float(hv[e]);
-            }
-            switch (c) {
-#define VCB_ADD4(I) case I: s[I][0] += x[0]; s[I][1] += x[1]; s[I][2] += x[2]; s[I][3] += x[3]; break;
-                VCB_ADD4(0) VCB_ADD4(1) VCB_ADD4(2) VCB_ADD4(3) VCB_ADD4(4) VCB_ADD4(5) VCB_ADD4(6) VCB_ADD4(7)
-#undef VCB_ADD4
+        for (int i = 0; i < 8; ++i) {
+            unsigned m = __ballot_sync(0xffffffffu, mine == i);
+            while (m) {
+                const int t = t0 + __ffs(m) - 1;
+                m &= m - 1;
+                float x[4];
+                const uint8_t* xr = xs + t * RB;
+                if constexpr (sizeof(T) == 4) {
+                    const float4 v = *reinterpret_cast<const float4*>(xr + ((lane ^ (t & (NCH - 1))) << 4));
+                    x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+                } else {
+                    const uint2 raw = *reinterpret_cast<const uint2*>(xr + (((lane >> 1) ^ (t & (NCH - 1))) << 4) +
+                                                                      (lane & 1) * 8);
+                    const T* hv = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) x[e] = to_float(hv[e]);
+                }
+#pragma unroll
+                for (int e = 0; e < 4; ++e) s[i][e] += x[e];
             }
         }
 #pragma unroll

@@ -178,8 +178,9 @@ __global__ void __launch_bounds__(256) cluster_assign_kernel(ClusterArgs a) {
 }
 
 // D == 128: the chunk's rows are staged in shared memory once (coalesced
-// 16-byte loads, 16-byte chunks XOR-swizzled by row so that a warp reading
-// one chunk of 32 rows hits every bank group), then
+// 16-byte cp.async copies, no register staging; 16-byte chunks XOR-swizzled
+// by row so that a warp reading one chunk of 32 rows hits every bank group),
+// then
 //   distances  thread t = tokens t % 128 and t % 128 + 128 in the two lanes
 //              of packed FMAs against a doubled centre table, half of the
 //              clusters per thread (t / 128); channels streamed in order from
@@ -218,23 +219,18 @@ __global__ void __launch_bounds__(256, 2) cluster_assign128_kernel(ClusterArgs a
     }
     if (tid < kMaxClusters) cnt[tid] = 0;
     const uint4* src = reinterpret_cast<const uint4*>(static_cast<const T*>(a.v) + (h * a.S + base) * 128);
-    {   // every load of the chunk in flight before the first store
+    {   // the chunk straight into shared memory (cp.async, no register staging)
         constexpr int kPer = kChunk * NCH / 256;
-        constexpr int kRound = kPer < 16 ? kPer : 16;
 #pragma unroll
-        for (int u0 = 0; u0 < kPer; u0 += kRound) {
-            uint4 buf[kRound];
-#pragma unroll
-            for (int u = 0; u < kRound; ++u) {
-                const int g = tid + 256 * (u0 + u);
-                if (g / NCH < nvalid) buf[u] = __ldg(src + g);
-            }
-#pragma unroll
-            for (int u = 0; u < kRound; ++u) {
-                const int g = tid + 256 * (u0 + u), r = g / NCH, k = g % NCH;
-                if (r < nvalid) *reinterpret_cast<uint4*>(xs + r * RB + ((k ^ (r & (NCH - 1))) << 4)) = buf[u];
+        for (int u = 0; u < kPer; ++u) {
+            const int g = tid + 256 * u, r = g / NCH, k = g % NCH;
+            if (r < nvalid) {
+                const uint32_t dst = smem_u32(xs + r * RB + ((k ^ (r & (NCH - 1))) << 4));
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
+                             ::"r"(dst), "l"(__cvta_generic_to_global(src + g)) : "memory");
             }
         }
+        asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
     }
     __syncthreads();
     if (tid < count) {

@@ -4,8 +4,9 @@
 // gathered V in PyTorch, cuda_backend.py:51).
 //
 // One CTA per (head, 128-token tile): the tile's tokens are gathered through
-// the permutation with coalesced row loads into shared memory (staged in the
-// input type: 32 KB for bf16 / fp16, so more CTAs fit per SM), then
+// the permutation with coalesced 16-byte cp.async row copies into shared
+// memory (staged in the input type: 32 KB for bf16 / fp16, so more CTAs fit
+// per SM), then
 // thread c owns channel c: the finiteness check, the block mean (four
 // interleaved partial sums in tile order, see below), residual, per-channel
 // scale with the mean-dtype finite-storage guard, E4M3 residual written
@@ -38,26 +39,23 @@ __global__ void __launch_bounds__(128) vprep_kernel(const T* __restrict__ v, int
     if ((int)threadIdx.x < cnt) toks[threadIdx.x] = pi ? (int64_t)pi[h * S + s0 + threadIdx.x] : s0 + threadIdx.x;
     __syncthreads();
     if (dv == 128 && (reinterpret_cast<uintptr_t>(v) & 15) == 0) {
-        // Rows of 16-byte pieces, every load of the tile in flight at once.
+        // Rows of 16-byte pieces copied straight into shared memory
+        // (cp.async, every copy of the tile in flight at once).  Rows past
+        // the end of a ragged tile are not copied; nothing reads them.
         constexpr int E = 16 / (int)sizeof(T);        // elements per piece
         constexpr int NP = 128 / E;                   // pieces per row
         constexpr int kPer = kTile * NP / 128;        // pieces per thread
-        constexpr int kRound = kPer < 16 ? kPer : 16;
 #pragma unroll
-        for (int u0 = 0; u0 < kPer; u0 += kRound) {
-            uint4 buf[kRound];
-#pragma unroll
-            for (int u = 0; u < kRound; ++u) {
-                const int g = threadIdx.x + 128 * (u0 + u), j = g / NP, k = g % NP;
-                buf[u] = j < cnt ? __ldg(reinterpret_cast<const uint4*>(v + (h * S + toks[j]) * 128) + k)
-                                 : make_uint4(0u, 0u, 0u, 0u);
-            }
-#pragma unroll
-            for (int u = 0; u < kRound; ++u) {
-                const int g = threadIdx.x + 128 * (u0 + u), j = g / NP, k = g % NP;
-                *reinterpret_cast<uint4*>(tile + j * 128 + k * E) = buf[u];
+        for (int u = 0; u < kPer; ++u) {
+            const int g = threadIdx.x + 128 * u, j = g / NP, k = g % NP;
+            if (j < cnt) {
+                const uint4* src = reinterpret_cast<const uint4*>(v + (h * S + toks[j]) * 128) + k;
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
+                             ::"r"(smem_u32(tile + j * 128 + k * E)), "l"(__cvta_generic_to_global(src))
+                             : "memory");
             }
         }
+        asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
     } else
     for (int j = warp; j < kTile; j += 4) {
         const T* row = v + (h * S + toks[j < cnt ? j : 0]) * dv;

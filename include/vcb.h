@@ -45,7 +45,7 @@ enum vcb_dtype { VCB_F32 = 0, VCB_F16 = 1, VCB_BF16 = 2 };
 /* Bits of the device status word that kernels set (see vcb_read_status). */
 enum vcb_device_flags {
     VCB_FLAG_NONFINITE = 1,         /* a Q, K or V element was NaN or Inf */
-    VCB_FLAG_TIMEOUT = 2,           /* a bounded wait in the attention kernel expired */
+    VCB_FLAG_TIMEOUT = 2,           /* a bounded wait in the attention kernel (or vcb_wait_selftest) expired */
     VCB_FLAG_INTERNAL = 4           /* a device-side layout check failed; nothing was computed */
 };
 
@@ -197,6 +197,17 @@ VCB_API int vcb_forward(const vcb_forward_args* args, void* stream);
 
 /* Waits for `stream`, then reads the device status word into *flags. */
 VCB_API int vcb_read_status(const int32_t* status, void* stream, int32_t* flags);
+
+/* Self-test of the attention kernel's bounded waits; no reference
+ * counterpart (the reference's waits are host-side cuBLASLt calls).  One CTA
+ * holds tensor memory and a 1 KB bulk copy of src (device, 16-byte aligned)
+ * in flight, and four warps wait on a barrier phase that only `complete`
+ * finishes.  Without it every wait gives up after the kernels' 2 s limit; the
+ * CTA drains its copy, frees its tensor memory and sets VCB_FLAG_TIMEOUT in
+ * *status (nullable), as an attention CTA does.  report: device, 4 x int32,
+ * zeroed by the call: waits that gave up, waits that completed, 1 when the
+ * drained copy equals src, elapsed milliseconds. */
+VCB_API int vcb_wait_selftest(int complete, const void* src, int32_t* status, int32_t* report, void* stream);
 
 #ifdef __cplusplus
 }

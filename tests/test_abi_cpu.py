@@ -66,6 +66,10 @@ def test_null_pointers_are_rejected():
     a = _abi.AttnArgs(heads=1, sq=1, sk=1, dv=1, q_block=128, k_quant_block=256, kv_block=128, scale=1.0)
     assert lib.vcb_attention_fp8(ctypes.byref(a), None) == _abi.VCB_ERR_INVALID_ARGUMENT
     assert lib.vcb_expcast_codes(None, None, -1, None) == _abi.VCB_ERR_INVALID_ARGUMENT
+    assert lib.vcb_wait_selftest(0, None, None, None, None) == _abi.VCB_ERR_INVALID_ARGUMENT
+    # a misaligned copy source is refused before any CUDA call
+    assert lib.vcb_wait_selftest(0, 8, None, 16, None) == _abi.VCB_ERR_INVALID_ARGUMENT
+    assert "aligned" in _abi.last_error(lib)
 
 
 def test_check_raises_value_error_for_invalid_arguments():

@@ -309,6 +309,14 @@ int vcb_forward(const vcb_forward_args* a, void* stream) {
     return attn_run(&at, st);
 }
 
+int vcb_wait_selftest(int complete, const void* src, int32_t* status, int32_t* report, void* stream) {
+    VCB_REQUIRE(src && report, "src and report must be non-null");
+    VCB_REQUIRE(aligned16(src), "src must be 16-byte aligned");
+    int rc = require_sm100(nullptr);
+    if (rc) return rc;
+    return wait_selftest_run(complete, src, status, report, static_cast<cudaStream_t>(stream));
+}
+
 int vcb_read_status(const int32_t* status, void* stream, int32_t* flags) {
     VCB_REQUIRE(status && flags, "status and flags must be non-null");
     cudaStream_t st = static_cast<cudaStream_t>(stream);

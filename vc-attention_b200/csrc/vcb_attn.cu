@@ -611,6 +611,63 @@ int launch(const Params& p, dim3 grid, cudaStream_t st) {
     return VCB_OK;
 }
 
+// Self-test of the bounded waits, with no GPU fault involved.  One CTA sets up
+// what an attention CTA holds when a wait expires: tensor memory, a bulk copy
+// in flight and a tcgen05 commit to drain.  Lane 0 of each of the four warps
+// then waits through mbar_wait on a barrier phase that only `complete`
+// finishes.  Without it the first wait to pass kWaitLimitNs raises the abort
+// flag and the other warps give up on seeing it.  The CTA then runs the
+// attention kernel's teardown: drain the copy and the commit, free tensor
+// memory, set VCB_FLAG_TIMEOUT.  report: [0] waits that gave up, [1] waits
+// that completed, [2] 1 when the drained copy equals src, [3] elapsed ms.
+__global__ void __launch_bounds__(128, 1)
+    wait_selftest_kernel(int complete, const int32_t* __restrict__ src, int32_t* status, int32_t* report) {
+    __shared__ __align__(128) int32_t buf[256];
+    __shared__ __align__(8) uint64_t bars[3];   // 0: the awaited phase, 1: the copy, 2: the tcgen05 drain
+    __shared__ int abort_flag;
+    __shared__ uint32_t tmem_slot;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint64_t t0 = globaltimer();
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < 3; ++i) mbar_init(&bars[i], 1);
+        abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(&tmem_slot, 32);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+    volatile int* abort = &abort_flag;
+    if (threadIdx.x == 0) {
+        mbar_arrive_expect_tx(&bars[1], (uint32_t)sizeof(buf));
+        bulk_load(buf, src, (uint32_t)sizeof(buf), &bars[1]);
+        if (complete) mbar_arrive(&bars[0]);
+    }
+    if (lane == 0) atomicAdd(&report[mbar_wait(&bars[0], 0, abort) ? 1 : 0], 1);
+    if (threadIdx.x == 0) {
+        mma_commit(&bars[2]);            // no MMA issued: arrives once earlier tcgen05 work is done
+        drain_wait(&bars[2], 0);
+    }
+    drain_wait(&bars[1], 0);             // no copy may land after the CTA exits
+    int same = 1;
+    for (int i = threadIdx.x; i < 256; i += 128) same &= buf[i] == src[i];
+    tc_fence_before();
+    same = __syncthreads_and(same);
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 32);
+    }
+    if (threadIdx.x == 0) {
+        report[2] = same;
+        report[3] = (int32_t)((globaltimer() - t0) / 1000000ull);
+        if (*abort) flag_status(status, VCB_FLAG_TIMEOUT);
+    }
+}
+
 }  // namespace
 
 int attn_run(const vcb_attn_args* a, cudaStream_t st) {
@@ -641,6 +698,13 @@ int attn_run(const vcb_attn_args* a, cudaStream_t st) {
     const dim3 grid((unsigned)((a->sq + kBM - 1) / kBM), (unsigned)a->heads);
     if (a->expcast) return a->has_mean ? launch<true, true>(p, grid, st) : launch<true, false>(p, grid, st);
     return a->has_mean ? launch<false, true>(p, grid, st) : launch<false, false>(p, grid, st);
+}
+
+int wait_selftest_run(int complete, const void* src, int32_t* status, int32_t* report, cudaStream_t st) {
+    VCB_CUDA(cudaMemsetAsync(report, 0, 4 * sizeof(int32_t), st));
+    wait_selftest_kernel<<<1, 128, 0, st>>>(complete, static_cast<const int32_t*>(src), status, report);
+    VCB_CUDA(cudaGetLastError());
+    return VCB_OK;
 }
 
 }  // namespace vcb

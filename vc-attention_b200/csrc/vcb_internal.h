@@ -18,6 +18,7 @@ int group_run(const vcb_group_args* p, cudaStream_t st);
 
 // vcb_attn.cu
 int attn_run(const vcb_attn_args* p, cudaStream_t st);
+int wait_selftest_run(int complete, const void* src, int32_t* status, int32_t* report, cudaStream_t st);
 
 // vcb_expcast.cu
 int expcast_run(const float* x, uint8_t* codes, int64_t n, cudaStream_t st);

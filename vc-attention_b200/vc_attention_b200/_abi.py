@@ -85,6 +85,7 @@ SIGNATURES = {
     "vcb_forward_workspace": (c_size_t, [ctypes.POINTER(ForwardArgs)]),
     "vcb_forward": (c_int, [ctypes.POINTER(ForwardArgs), c_void_p]),
     "vcb_read_status": (c_int, [c_void_p, c_void_p, ctypes.POINTER(ctypes.c_int32)]),
+    "vcb_wait_selftest": (c_int, [c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
 }
 
 _lib = None

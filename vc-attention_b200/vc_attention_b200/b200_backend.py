@@ -215,6 +215,28 @@ def build_info():
     return json.loads(_extension().vcb_build_info().decode())
 
 
+def wait_selftest(complete=False, device="cuda:0"):
+    """Runs the self-test of the attention kernel's bounded waits
+    (``vcb_wait_selftest``) and returns its report and the device status word.
+    With ``complete=False`` the awaited phase never completes: the kernel gives
+    up after its 2 s limit, drains, frees tensor memory and sets the timeout
+    flag; ``raise_for_status(result["status"])`` then raises RuntimeError."""
+    device = torch.device(device)
+    if device.type != "cuda" or torch.cuda.get_device_capability(device) != (10, 0):
+        raise RuntimeError("wait_selftest requires a B200-class GPU (compute capability 10.0)")
+    lib = _extension()
+    gen = torch.Generator().manual_seed(7)
+    src = torch.randint(-2**31, 2**31 - 1, (256,), dtype=torch.int32, generator=gen).to(device)
+    status = torch.zeros(1, dtype=torch.int32, device=device)
+    report = torch.empty(4, dtype=torch.int32, device=device)
+    with torch.cuda.device(device):
+        _abi.check(lib, lib.vcb_wait_selftest(int(bool(complete)), src.data_ptr(), status.data_ptr(),
+                                              report.data_ptr(), _stream(device)))
+    gave_up, completed, copy_intact, elapsed_ms = report.tolist()
+    return {"gave_up": gave_up, "completed": completed, "copy_intact": bool(copy_intact),
+            "elapsed_ms": elapsed_ms, "status": status}
+
+
 def preflight(device="cuda:0"):
     """Fail loudly unless ExpCast bytes and the fused FP8 path work (cuda_backend.py:69-88)."""
     from .core import Config, attention

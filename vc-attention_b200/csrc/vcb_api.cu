@@ -113,7 +113,7 @@ const char* vcb_build_info(void) {
            ", \"fully_fused_attention\": true, \"numerical_contract_version\": 2"
            ", \"expcast_rounding\": \"FP32 FMA then RNE\""
            ", \"value_mean_storage\": \"mu / per-channel V scale at configured mean dtype\""
-           ", \"row_mass\": \"ExpCast: tensor-core sum of decoded P; otherwise FP32 sum of exp\"}";
+           ", \"row_mass\": \"FP32 sum of the row's decoded ExpCast P, or of its exp values\"}";
 }
 
 size_t vcb_last_error(char* buf, size_t size) {

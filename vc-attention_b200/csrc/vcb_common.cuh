@@ -64,6 +64,26 @@ __device__ __forceinline__ void load8(const __nv_bfloat16* p, float* o) {
     for (int i = 0; i < 4; ++i) { float2 f = __bfloat1622float2(h[i]); o[2 * i] = f.x; o[2 * i + 1] = f.y; }
 }
 
+// The same eight elements as channel pairs: o[i] = (p[2i], p[2i+1]).
+__device__ __forceinline__ void load8x2(const float* p, float2* o) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+    o[0] = make_float2(a.x, a.y); o[1] = make_float2(a.z, a.w);
+    o[2] = make_float2(b.x, b.y); o[3] = make_float2(b.z, b.w);
+}
+__device__ __forceinline__ void load8x2(const __half* p, float2* o) {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o[i] = __half22float2(h[i]);
+}
+__device__ __forceinline__ void load8x2(const __nv_bfloat16* p, float2* o) {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o[i] = __bfloat1622float2(h[i]);
+}
+
 __device__ __forceinline__ bool finite_f(float x) { return fabsf(x) <= 3.402823466e38f; }
 
 // max that returns NaN when either input is NaN (max.NaN), so a block's amax
@@ -71,6 +91,12 @@ __device__ __forceinline__ bool finite_f(float x) { return fabsf(x) <= 3.4028234
 __device__ __forceinline__ float fmax_nan(float a, float b) {
     float d;
     asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+    return d;
+}
+// The three-input form (sm_100): NaN when any input is NaN.
+__device__ __forceinline__ float fmax3_nan(float a, float b, float c) {
+    float d;
+    asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
     return d;
 }
 

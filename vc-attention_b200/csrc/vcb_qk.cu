@@ -7,6 +7,8 @@
 //   K mean: chunks of kKsumChunk rows; inside a chunk row r goes to lane
 //   r % kKsumLanes, lanes sum their rows in increasing order, the chunk sum
 //   adds lanes in order, the head total adds chunks in order, then / S.
+#include <type_traits>
+
 #include "vcb_internal.h"
 
 namespace vcb {
@@ -131,17 +133,16 @@ __device__ __forceinline__ bool transform_row(const RowArgs& a, int64_t h, int64
 // one row, the lower lane channels [0, 64), the upper lane [64, 128).  The
 // butterflies with stride 1..32 stay inside a half; the stride-64 stage
 // exchanges halves with one shuffle per element and still computes
-// (left + right, left - right) on the same operands.
-// FIX: D == 128 with the 128-point Hadamard, every bound known at compile time.
-template <typename T, bool FIX>
-__device__ __forceinline__ void transform_half(const RowArgs& a, int64_t h, int64_t r, bool valid, int half,
-                                               const float* smean, float (&x)[64], int64_t tok_hint = -1) {
+// (left + right, left - right) on the same operands.  `tok` is the input row
+// (row r through the permutation).
+template <typename T>
+__device__ __forceinline__ void transform_half(const RowArgs& a, int64_t h, int64_t tok, bool valid, int half,
+                                               const float* smean, float (&x)[64]) {
     const int c0 = 64 * half;
-    const int D = FIX ? 128 : a.D;
-    const int width = FIX ? 128 : a.width;
-    const bool hadamard = FIX ? true : a.hadamard != 0;
+    const int D = a.D;
+    const int width = a.width;
+    const bool hadamard = a.hadamard != 0;
     if (valid) {
-        const int64_t tok = tok_hint >= 0 ? tok_hint : a.pi ? (int64_t)a.pi[h * a.S + r] : r;
         const T* src = static_cast<const T*>(a.x) + (h * a.S + tok) * D;
         if (D == 128) {
 #pragma unroll
@@ -181,11 +182,66 @@ __device__ __forceinline__ void transform_half(const RowArgs& a, int64_t h, int6
                 x[c] = half == 0 ? x[c] + other : other - x[c];
             }
         }
-        const float norm = FIX ? 0.08838834764831845f : a.norm;     // fp32(128^-0.5)
 #pragma unroll
         for (int c = 0; c < 64; ++c)
-            if (c0 + c < width) x[c] = x[c] * norm;
+            if (c0 + c < width) x[c] = x[c] * a.norm;
     }
+}
+
+// transform_half for D == 128 with the 128-point Hadamard, in packed FP32:
+// the half row is 32 channel pairs, and the demean, the butterflies from
+// stride 2 on, the stride-64 exchange and the normalisation are add / fma /
+// mul .f32x2, each lane rounded once like the scalar form.  l - r is computed
+// as fma(r, -1, l): the product is exact, so the result is RN(l - r) with the
+// same sign of zero.
+template <typename T>
+__device__ __forceinline__ void transform_half128(const RowArgs& a, int64_t h, int64_t tok, bool valid, int half,
+                                                  const float* smean, float2 (&x)[32]) {
+    const int c0 = 64 * half;
+    const float2 neg1 = make_float2(-1.0f, -1.0f);
+    if (valid) {
+        const T* src = static_cast<const T*>(a.x) + (h * a.S + tok) * 128 + c0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) load8x2(src + 8 * i, x + 4 * i);
+        if (smean) {
+            const float2* m2 = reinterpret_cast<const float2*>(smean + c0);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) x[i] = ffma2(m2[i], neg1, x[i]);
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) x[i] = make_float2(0.0f, 0.0f);
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {          // stride 1: inside one pair
+        const float l = x[i].x, r = x[i].y;
+        x[i] = make_float2(l + r, l - r);
+    }
+#pragma unroll
+    for (int s = 1; s < 32; s <<= 1) {      // strides 2 .. 32: s pairs apart
+#pragma unroll
+        for (int base = 0; base < 32; base += 2 * s) {
+#pragma unroll
+            for (int t = 0; t < s; ++t) {
+                const float2 l = x[base + t], r = x[base + s + t];
+                x[base + t] = fadd2(l, r);
+                x[base + s + t] = ffma2(r, neg1, l);
+            }
+        }
+    }
+    // stride 64 across the lane pair: half 0 keeps left + right = fma(x, 1,
+    // other), half 1 left - right = fma(x, -1, other)
+    const float sg = half ? -1.0f : 1.0f;
+    const float2 sg2 = make_float2(sg, sg);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        const float2 other = make_float2(__shfl_xor_sync(0xffffffffu, x[i].x, 16),
+                                         __shfl_xor_sync(0xffffffffu, x[i].y, 16));
+        x[i] = ffma2(x[i], sg2, other);
+    }
+    const float2 norm2 = make_float2(0.08838834764831845f, 0.08838834764831845f);   // fp32(128^-0.5)
+#pragma unroll
+    for (int i = 0; i < 32; ++i) x[i] = fmul2(x[i], norm2);
 }
 
 // 64 E4M3 bytes of a half row: x / scale as div_by(x * pre, bdiv, rdiv)
@@ -212,12 +268,40 @@ __device__ __forceinline__ void encode_half(const float (&x)[64], int c0, int W,
     }
 }
 
+// encode_half over the 32 channel pairs of transform_half128: div_by in
+// packed FP32 (fma(q, -b, x) is fma(-q, b, x): the same exact product).
+template <bool PRE>
+__device__ __forceinline__ void encode_half128(const float2 (&x)[32], float pre, float bdiv, float rdiv,
+                                               uint4* dst) {
+    const float2 y2 = make_float2(rdiv, rdiv), nb2 = make_float2(-bdiv, -bdiv), p2 = make_float2(pre, pre);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        uint32_t w[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            uint32_t b[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                float2 v = x[8 * q + 2 * k + e];
+                if (PRE) v = fmul2(v, p2);
+                const float2 qq = fmul2(v, y2);
+                const float2 rr = ffma2(qq, nb2, v);
+                const float2 d = ffma2(rr, y2, qq);
+                b[e] = e4m3x2(d.x, d.y);
+            }
+            w[k] = b[0] | (b[1] << 16);
+        }
+        dst[q] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
 // One CTA per quantisation block, two threads per row, 256 rows per pass.
 // Blocks of at most 256 rows keep the transformed halves in registers from
 // the amax to the encode; larger blocks re-read and re-transform in pass 2.
+// FIX: D == 128 with the 128-point Hadamard, on the packed helpers.
 template <typename T, bool FIX>
 __global__ void __launch_bounds__(512) qk_quant_kernel(RowArgs a) {
-    __shared__ float smean[128];
+    __shared__ __align__(16) float smean[128];
     __shared__ int32_t stok[256];
     __shared__ float red[16];
     __shared__ float sdiv[3];
@@ -237,7 +321,17 @@ __global__ void __launch_bounds__(512) qk_quant_kernel(RowArgs a) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int half = lane >> 4;
     const int rows_per_pass = nthr / 2;
-    float x[64];
+    using Half = std::conditional_t<FIX, float2[32], float[64]>;
+    Half x;
+    // the input row of block row rl (valid rows only)
+    auto token = [&](int rl, int64_t r) -> int64_t {
+        if (!a.pi) return r;
+        return single ? (int64_t)stok[rl] : (int64_t)a.pi[h * a.S + r];
+    };
+    auto transform = [&](int64_t tok, bool valid) {
+        if constexpr (FIX) transform_half128<T>(a, h, tok, valid, half, sm, x);
+        else transform_half<T>(a, h, tok, valid, half, sm, x);
+    };
     // max.NaN keeps a NaN (from a NaN or infinite input, or Inf - Inf in the
     // transform) all the way to the block maximum, which is then the
     // finiteness check of every input row of the block
@@ -246,11 +340,15 @@ __global__ void __launch_bounds__(512) qk_quant_kernel(RowArgs a) {
         const int rl = base + warp * 16 + (lane & 15);
         const int64_t r = r0 + rl;
         const bool valid = rl < a.block && r < a.S;
-        const int64_t tok = single ? (a.pi ? (valid ? (int64_t)stok[rl] : 0) : r) : -1;
-        transform_half<T, FIX>(a, h, r, valid, half, sm, x, tok);
+        transform(valid ? token(rl, r) : 0, valid);
+        if constexpr (FIX) {
 #pragma unroll
-        for (int c = 0; c < 64; ++c)
-            if (64 * half + c < W) amax = fmax_nan(amax, fabsf(x[c]));
+            for (int i = 0; i < 32; ++i) amax = fmax3_nan(amax, fabsf(x[i].x), fabsf(x[i].y));
+        } else {
+#pragma unroll
+            for (int c = 0; c < 64; ++c)
+                if (64 * half + c < W) amax = fmax_nan(amax, fabsf(x[c]));
+        }
     }
     for (int o = 16; o > 0; o >>= 1) amax = fmax_nan(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     if (lane == 0) red[warp] = amax;
@@ -273,7 +371,7 @@ __global__ void __launch_bounds__(512) qk_quant_kernel(RowArgs a) {
         const int rl = base + warp * 16 + (lane & 15);
         const int64_t r = r0 + rl;
         const bool valid = rl < a.block && r < a.S;
-        if (!single) transform_half<T, FIX>(a, h, r, valid, half, sm, x);   // warp-uniform
+        if (!single) transform(valid ? token(rl, r) : 0, valid);   // warp-uniform
         if (rl >= a.block || r >= a.S_pad) continue;
         uint4* dst = reinterpret_cast<uint4*>(a.payload + (h * a.S_pad + r) * 128 + 64 * half);
         if (!valid) {
@@ -281,8 +379,13 @@ __global__ void __launch_bounds__(512) qk_quant_kernel(RowArgs a) {
             for (int q = 0; q < 4; ++q) dst[q] = make_uint4(0u, 0u, 0u, 0u);
             continue;
         }
-        if (pre == 1.0f) encode_half<false>(x, 64 * half, W, pre, bdiv, rdiv, dst);   // block-uniform
-        else encode_half<true>(x, 64 * half, W, pre, bdiv, rdiv, dst);
+        if constexpr (FIX) {
+            if (pre == 1.0f) encode_half128<false>(x, pre, bdiv, rdiv, dst);   // block-uniform
+            else encode_half128<true>(x, pre, bdiv, rdiv, dst);
+        } else {
+            if (pre == 1.0f) encode_half<false>(x, 64 * half, W, pre, bdiv, rdiv, dst);
+            else encode_half<true>(x, 64 * half, W, pre, bdiv, rdiv, dst);
+        }
     }
 }
 

@@ -24,6 +24,7 @@ chunk (key ``(layer_id, first_head)``) with the usual refresh schedule.
 from __future__ import annotations
 
 import math
+import threading
 
 import torch
 
@@ -33,6 +34,7 @@ from .core import Config, LayoutCache, _validate
 _BUFFER_SETS = 8          # chunk-sized input sets in the device ring
 _COMPUTE_STREAMS = 3      # compute streams the chunks rotate over
 _streams = {}
+_streams_lock = threading.Lock()
 
 
 def _chunks(n, size):
@@ -43,11 +45,12 @@ def _pipeline_streams(device):
     """(h2d, d2h, [compute...]) for ``device``, made once and reused, so the
     caching allocator keeps serving the same per-stream pools."""
     key = device.index if device.index is not None else torch.cuda.current_device()
-    if key not in _streams:
-        with torch.cuda.device(key):
-            _streams[key] = (torch.cuda.Stream(), torch.cuda.Stream(),
-                             [torch.cuda.Stream() for _ in range(_COMPUTE_STREAMS)])
-    return _streams[key]
+    with _streams_lock:
+        if key not in _streams:
+            with torch.cuda.device(key):
+                _streams[key] = (torch.cuda.Stream(), torch.cuda.Stream(),
+                                 [torch.cuda.Stream() for _ in range(_COMPUTE_STREAMS)])
+        return _streams[key]
 
 
 @torch.no_grad()

@@ -64,6 +64,8 @@ QK_CASES = [
     (torch.bfloat16, 1, 256, 384, 128, 32, 128, False, True, False),
     (torch.float32, 2, 200, 300, 21, 96, 256, True, False, False),
     (torch.bfloat16, 1, 600, 5000, 128, 256, 4096, True, True, True),
+    (torch.float16, 2, 500, 900, 128, 64, 256, True, True, True),
+    (torch.bfloat16, 2, 100, 200, 128, 8, 16, True, True, True),     # blocks below one warp of rows
 ]
 
 

@@ -200,8 +200,158 @@ def run_reference(args, world, rank):
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
 
 
+def _e4m3(b):
+    return b.view(torch.float8_e4m3fn).float()
+
+
+@torch.no_grad()
+def rows_check(q, k, v, out, cfg, *, head, r0, pi, active, scale=D ** -0.5):
+    """Checks 128 rows of one head of a GPU forward on the GPU that ran it.
+
+    The reference's streaming loop (core.py:307-340) is evaluated with torch
+    in FP32 (no TF32) over the library's own prepared operands of that head
+    (E4M3 Q/K blocks and V tiles, whose bytes the GPU tests pin to the CPU
+    checker), with the reference's FP64-intermediate ExpCast encode
+    (core.py:60-68).  This needs no host-side checker, so it runs on every
+    rank of a multi-GPU job.  Returns relative RMSE and cosine against the
+    fused kernel's output rows."""
+    from vc_attention_b200 import stages
+
+    hs = slice(head, head + 1)
+    qh, kh, vh = (x[:, hs].contiguous() for x in (q, k, v))
+    ph = None if pi is None else pi[:, hs].contiguous()
+    q8, qs, k8, ks = stages.quantize_qk(qh, kh, pi=ph, q_block=cfg.q_block, k_quant_block=cfg.k_quant_block,
+                                        k_smooth=cfg.k_smooth, hadamard=cfg.qk_hadamard)
+    v8, meta = stages.prepare_v(vh, pi=ph, active=active, mean_dtype=cfg.mean_dtype)
+    sk, dv = k.shape[2], v.shape[3]
+    rows = torch.arange(r0, r0 + 128, device=q.device)
+    keys = torch.arange(sk, device=q.device)
+    qd = _e4m3(q8[0, rows]) * qs[0, rows // cfg.q_block][:, None]
+    kd = _e4m3(k8[0, :sk]) * ks[0, keys // cfg.k_quant_block][:, None]
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        m = torch.full((128, 1), -float("inf"), device=q.device)
+        den = torch.zeros((128, 1), device=q.device)
+        acc = torch.zeros((128, dv), device=q.device)
+        for j, s0 in enumerate(range(0, sk, 128)):
+            kt = kd[s0:s0 + 128]
+            s = (qd @ kt.T) * scale
+            newmax = torch.maximum(m, s.amax(-1, keepdim=True))
+            alpha = torch.exp(m - newmax)
+            shifted = s - newmax
+            if cfg.expcast:
+                code = (shifted.double() * 11.541560173034668 + 119.6500015258789).float()
+                p8 = torch.round(code).clamp(0, 120).to(torch.uint8).view(torch.float8_e4m3fn).float()
+                prob = p8 / 256.0
+            else:
+                prob = torch.exp(shifted)
+                p8 = (prob * 256.0).to(torch.float8_e4m3fn).float()
+            mass = prob.sum(-1, keepdim=True)
+            resid = _e4m3(v8[0, j, :dv, :kt.shape[0]]).T
+            contrib = (p8 @ resid / 256.0 + mass * meta[0, j, 1, :dv]) * meta[0, j, 0, :dv]
+            acc = alpha * acc + contrib
+            den = alpha * den + mass
+            m = newmax
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    ref = (acc / den).to(out.dtype).double().flatten()
+    got = out[0, head, r0:r0 + 128].double().flatten()
+    rel = float(((got - ref).square().mean() / ref.square().mean().clamp_min(1e-30)).sqrt())
+    cos = float(torch.dot(got, ref) / (got.norm() * ref.norm()).clamp_min(1e-8))
+    return {"relative_rmse": rel, "cosine": cos}
+
+
+def copy_ceiling_ms(hq, hk, hv, hout, device, reps=3):
+    """H2D of the step's inputs and D2H of its output alone (pinned host
+    memory, one stream per direction, both directions at once): the time
+    the e2e step could not beat even with the compute fully hidden."""
+    dq, dk, dv = (torch.empty(x.shape, dtype=x.dtype, device=device) for x in (hq, hk, hv))
+    do = torch.empty(hout.shape, dtype=hout.dtype, device=device)
+    up, down = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    best = float("inf")
+    for _ in range(reps):
+        torch.cuda.synchronize(device)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        cur = torch.cuda.current_stream(device)
+        s.record(cur)
+        up.wait_stream(cur)
+        down.wait_stream(cur)
+        with torch.cuda.stream(up):
+            for d, h in ((dq, hq), (dk, hk), (dv, hv)):
+                d.copy_(h, non_blocking=True)
+        with torch.cuda.stream(down):
+            hout.copy_(do, non_blocking=True)
+        cur.wait_stream(up)
+        cur.wait_stream(down)
+        e.record(cur)
+        e.synchronize()
+        best = min(best, s.elapsed_time(e))
+    return best
+
+
+def config4_object(args, world, rank, local):
+    """Configuration 4 inside the multi-GPU bench line: B1 H24 S131072 D128
+    bf16, combined mode at a refresh step, inputs sequence-sharded (S/N tokens
+    of all 24 heads per rank); one step is the seq->head all-to-all of Q/K/V
+    (NCCL), the forward on 24/N heads over all tokens, and the head->seq
+    all-to-all of the output (lightx2v.py:119, :138-139).  Times are CUDA
+    events, max over ranks; the check compares 128 rows of this rank's first
+    head with rows_check."""
+    from vc_attention_b200 import Config, LayoutCache, sharding
+    from vc_attention_b200.synthetic import make_qkv
+
+    heads, seq = 24, 131072
+    device = torch.device("cuda", local)
+    group = torch.distributed.group.WORLD
+    s = seq // world
+    q, k, v = (x[:, :, rank * s:(rank + 1) * s].contiguous() for x in make_qkv("c4", 2000, device=device))
+    cfg = Config(v_smooth=True, expcast=True)
+
+    def step(i):
+        cache = LayoutCache(cfg)
+        out, _ = sharding.attention_seq_sharded(q, k, v, cfg, group=group, cache=cache, step=0, total_steps=50,
+                                                request_id=i)
+        return out, cache
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    barrier(world)
+    s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record()
+    for i in range(args.steps):
+        out, cache = step(i)
+    e0.record()
+    e0.synchronize()
+    ms = sharding.max_over_ranks(s0.elapsed_time(e0) / args.steps)
+    s1, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s1.record()
+    for _ in range(args.steps):
+        hs = [sharding.seq_to_heads(x, group) for x in (q, k, v)]
+        sharding.heads_to_seq(hs[0], group)
+    e1.record()
+    e1.synchronize()
+    a2a_ms = sharding.max_over_ranks(s1.elapsed_time(e1) / args.steps)
+    # check: this rank's heads over all tokens, taken back from the sequence-sharded output
+    qh, kh, vh = (sharding.seq_to_heads(x, group) for x in (q, k, v))
+    oh = sharding.seq_to_heads(out, group)
+    pi = cache._states[0]["pi"]
+    chk = rows_check(qh, kh, vh, oh, cfg, head=0, r0=4096 + 128 * rank, pi=pi, active=True)
+    worst_rmse = sharding.max_over_ranks(chk["relative_rmse"])
+    worst_cos = -sharding.max_over_ranks(-chk["cosine"])
+    total = 4.0 * heads * seq * seq * 128
+    return {"workload": "c4: B1 H24 S131072 D128 bf16 combined, refresh step, sequence-sharded inputs",
+            "parallelism": f"Ulysses: seq->head all-to-all, {heads // world} heads per rank, head->seq all-to-all",
+            "ms_per_step": ms, "tflops_total": total / (ms * 1e-3) / 1e12,
+            "tflops_per_gpu": total / (ms * 1e-3) / 1e12 / world, "all_to_all_ms": a2a_ms,
+            "parity": {"rows": "128 rows of each rank's first head", "relative_rmse_max": worst_rmse,
+                       "cosine_min": worst_cos, "tolerance": {"relative_rmse": 1e-3, "cosine": 0.9999},
+                       "ok": worst_rmse <= 1e-3 and worst_cos >= 0.9999}}
+
+
 def run_ours(args, world, rank, local):
-    from vc_attention_b200 import Config, LayoutCache, attention_streamed, sharding, stages
+    from vc_attention_b200 import Config, LayoutCache, attention_streamed, check_streamed, sharding, stages
     from vc_attention_b200.b200_backend import forward, group_values
     from vc_attention_b200.synthetic import make_qkv
 
@@ -216,9 +366,12 @@ def run_ours(args, world, rank, local):
     status = torch.zeros(1, dtype=torch.int32, device=device)
     workspace = None
 
+    pi_step = None
+
     def step():
-        nonlocal workspace
+        nonlocal workspace, pi_step
         pi, _ = group_values(v, clusters=cfg.clusters, iterations=cfg.iterations)
+        pi_step = pi
         if workspace is None:
             import ctypes
             from vc_attention_b200 import _abi
@@ -271,29 +424,50 @@ def run_ours(args, world, rank, local):
     attn_ms = sharding.max_over_ranks(attn_ms)
     achieved = flops(h=h_loc) / (attn_ms * 1e-3) / 1e12
     peak = fp8_peak_tflops(device)
-    traffic = None
+    traffic, traffic_note = None, None
     tfile = ROOT / "profiles" / "attn_kernel_traffic.json"
     if tfile.exists():
-        traffic = json.loads(tfile.read_text()).get("bytes_per_launch_full_c3")
+        rec = json.loads(tfile.read_text())
+        traffic = rec["bytes_per_launch_full_c3"] * h_loc / H
+        traffic_note = (f"not measured in this run: DRAM bytes of one ncu capture ({rec['captured_case']}), "
+                        f"scaled per head to this rank's {h_loc} heads ({tfile.relative_to(ROOT)})")
+
+    # 128 rows of one head of the timed forward, checked on this GPU (max over ranks)
+    chk = rows_check(q, k, v, out, cfg, head=h_loc - 1, r0=128 * (37 + 11 * rank), pi=pi_step, active=True)
+    parity = {"rows": "128 query rows of each rank's last head, full K/V (replay semantics)",
+              "relative_rmse_max": sharding.max_over_ranks(chk["relative_rmse"]),
+              "cosine_min": -sharding.max_over_ranks(-chk["cosine"]),
+              "tolerance": {"relative_rmse": 1e-3, "cosine": 0.9999},
+              "reference": "core.py:307-340 in torch FP32 (FP64-intermediate ExpCast) over this library's "
+                           "prepared operands"}
+    parity["ok"] = parity["relative_rmse_max"] <= 1e-3 and parity["cosine_min"] >= 0.9999
 
     # end to end through the public API, host buffers in and out
     hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
     hout = torch.empty(q.shape, dtype=q.dtype).pin_memory()
     barrier(world)
-    e2e_ms = []
+    e2e_ms, e2e_stats = [], []
     for i in range(args.warmup + args.steps):
         torch.cuda.synchronize()
         barrier(world)
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
         # host in, host out: per-chunk H2D, forwards on rotating compute streams, D2H
-        attention_streamed(hq, hk, hv, cfg, cache=LayoutCache(cfg), step=0, total_steps=50, request_id=i,
-                           device=device, out=hout, synchronize=False)
+        _, st = attention_streamed(hq, hk, hv, cfg, cache=LayoutCache(cfg), step=0, total_steps=50,
+                                   request_id=i, device=device, out=hout, synchronize=False)
         e.record()
         e.synchronize()
+        e2e_stats.append(st)
         if i >= args.warmup:
             e2e_ms.append(s.elapsed_time(e))
+    # every e2e step's device status is read after the timed loop: a step
+    # whose kernels flagged non-finite input, an expired wait or a failed
+    # layout check invalidates the e2e figure (check_streamed raises)
+    for st in e2e_stats:
+        check_streamed(st)
     e2e = sharding.max_over_ranks(sum(e2e_ms) / len(e2e_ms))
+    ceiling = sharding.max_over_ranks(copy_ceiling_ms(hq, hk, hv, hout, device))
+    c4 = config4_object(args, world, rank, local) if world > 1 and not args.no_config4 else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -301,7 +475,8 @@ def run_ours(args, world, rank, local):
     if rank == 0:
         nbytes = q.numel() * q.element_size()
         line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "metric": METRIC, "value": value, "value_per_gpu": value / world, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "e4m3 (bf16 in/out, fp32 accumulate)", "data": "synthetic",
             "config": dict(CONFIG, global_batch=1,
@@ -310,15 +485,23 @@ def run_ours(args, world, rank, local):
             "e2e": {"value": flops() / (e2e * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": e2e,
                     "ms_per_step_median": statistics.median(e2e_ms),
                     "steps_ms": [round(t, 3) for t in e2e_ms],
-                    "h2d_bytes_per_step": 3 * nbytes, "d2h_bytes_per_step": nbytes},
+                    "h2d_bytes_per_step": 3 * nbytes, "d2h_bytes_per_step": nbytes,
+                    "status_checked": True,
+                    "copy_ceiling_ms": ceiling,
+                    "frac_of_copy_ceiling": ceiling / e2e,
+                    "copy_ceiling": "the same H2D and D2H bytes alone, pinned, one stream per direction, "
+                                    "max over ranks"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved / peak, "traffic": traffic, "kernel": "attn_kernel",
+                         "frac": achieved / peak, "traffic": traffic, "traffic_source": traffic_note,
+                         "kernel": "attn_kernel",
                          "kernel_ms": attn_ms,
                          "peak_source": "measured in this run: torch._scaled_mm E4M3 8192^3 burst",
                          "frac_of_spec_4500": achieved / 4500.0},
             "cpu_baseline": cpu,
             "clocks": clocks.summary(),
             "gpu_launches": LAUNCHES_PER_STEP * args.steps,
+            "parity": parity,
+            "config4": c4,
         }
         print(json.dumps(line))
 
@@ -457,6 +640,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-config4", action="store_true", help="skip the configuration-4 object at N > 1")
     ap.add_argument("--case", choices=("attn", "prep", "ulysses", "schedule"),
                     help="attn / prep: small single-GPU cases for profilers; ulysses: config 4 "
                          "sequence-sharded; schedule: config 5's 50-step loop in every mode")

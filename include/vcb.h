@@ -7,7 +7,8 @@
  * buffer (inputs, outputs, scratch) belongs to the caller; the library
  * allocates no device memory and keeps no per-call state.  All work is
  * enqueued on the stream the caller passes (bindings.cpp:176 uses the
- * current PyTorch stream the same way); nothing synchronises the device.
+ * current PyTorch stream the same way); nothing synchronises the device,
+ * and only vcb_read_status waits for the caller's stream.
  *
  * Tensors are contiguous, batch and heads flattened: [heads, tokens, dim].
  * Functions return VCB_OK or a VCB_ERR_* code; vcb_last_error() gives the
@@ -108,7 +109,8 @@ VCB_API int vcb_quantize_qk(const vcb_qk_args* args, void* stream);
  * bytes with k_smooth) fail with VCB_ERR_INVALID_ARGUMENT.  All calls share
  * the array, so calls that overlap on the GPU race.  The first call on a
  * device looks up the array's address and should come before any stream
- * capture.  This entry point has no counterpart in the reference. */
+ * capture; after a device reset the first call in the new context looks it
+ * up again.  This entry point has no counterpart in the reference. */
 VCB_API int vcb_quantize_qk_static(const vcb_qk_args* args, void* stream);
 
 /* ---- V clustering (Lloyd + stable permutation) ---------------------------- */
@@ -171,6 +173,26 @@ typedef struct {
  * online softmax with ExpCast and V-mean recovery, output in out_dtype */
 VCB_API int vcb_attention_fp8(const vcb_attn_args* args, void* stream);
 
+/* Diagnostic dump of the fused kernel's softmax for one (head, 128-row query
+ * tile): KV tiles [tile_begin, tile_begin + tile_count) of that CTA write the
+ * raw FP32 logits s = q8 . k8 (masked keys of a ragged last tile as -inf),
+ * the 128 P bytes per row exactly as the PV MMA reads them (ExpCast codes, or
+ * E4M3(exp * 256)), and per row: the running max m after the tile, the
+ * encode's slope A and offset B (P = rne(fma(s, A, B) * 2^24) with ExpCast,
+ * in units of 2^-24), and the rescale factor alpha.  The attention itself
+ * runs in full as in vcb_attention_fp8.  Used by the tests to count the
+ * ExpCast bytes that differ from the reference's FP64-intermediate encode of
+ * (S - m) (core.py:60-68, :326-328); no reference counterpart. */
+typedef struct {
+    int64_t head, q_tile;
+    int tile_begin, tile_count;
+    float* logits;          /* [tile_count, 128, 128] */
+    uint8_t* codes;         /* [tile_count, 128, 128] */
+    float* rowstat;         /* [tile_count, 128, 4]: m, A, B, alpha */
+} vcb_attn_probe;
+
+VCB_API int vcb_attention_fp8_probe(const vcb_attn_args* args, const vcb_attn_probe* probe, void* stream);
+
 /* ---- whole forward ----------------------------------------------------------- */
 typedef struct {
     const void* q; const void* k; const void* v;
@@ -195,7 +217,9 @@ VCB_API size_t vcb_forward_workspace(const vcb_forward_args* args);
  * scale, k_smooth, hadamard) (bindings.cpp:100-178) */
 VCB_API int vcb_forward(const vcb_forward_args* args, void* stream);
 
-/* Waits for `stream`, then reads the device status word into *flags. */
+/* Reads the device status word into *flags: one device-to-host copy ordered
+ * on `stream` (not on the legacy default stream), then a wait for `stream`
+ * only.  The one call of this library that blocks the host. */
 VCB_API int vcb_read_status(const int32_t* status, void* stream, int32_t* flags);
 
 /* Self-test of the attention kernel's bounded waits; no reference

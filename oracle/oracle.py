@@ -55,6 +55,7 @@ def lib():
             L.vco_e4m3_decode_n.argtypes = [_u8p, _f32p, i64]
             L.vco_expcast_fma.argtypes = [_f32p, _u8p, i64]
             L.vco_expcast_fp64.argtypes = [_f32p, _u8p, i64]
+            L.vco_fused_codes.argtypes = [_f32p, _f32p, _f32p, i64, _u8p]
             L.vco_hadamard_rows.argtypes = [_f32p, i64, i32, _f32p]
             L.vco_k_mean.argtypes = [_f32p, i64, i64, i32, _f32p]
             L.vco_quant_blocks.argtypes = [_f32p, i64, i64, i32, i32, i64, _u8p, _f32p]
@@ -99,6 +100,16 @@ def expcast_codes(x, *, fp64=True):
     out = np.empty(x.shape, np.uint8)
     fn = lib().vco_expcast_fp64 if fp64 else lib().vco_expcast_fma
     fn(x.reshape(-1), out.reshape(-1), x.size)
+    return out
+
+
+def fused_codes(s, a, b):
+    """The fused attention kernel's encode (vc_oracle.c vco_fused_codes):
+    RNE(fmaf(s, a, b) * 2^24), negatives to 0; a, b broadcast against s."""
+    s = _f32(s)
+    a, b = (_f32(np.broadcast_to(x, s.shape)) for x in (a, b))
+    out = np.empty(s.shape, np.uint8)
+    lib().vco_fused_codes(s.reshape(-1), a.reshape(-1), b.reshape(-1), s.size, out.reshape(-1))
     return out
 
 

@@ -112,6 +112,21 @@ void vco_expcast_fma(const float* x, uint8_t* out, int64_t n) {
     for (int64_t i = 0; i < n; ++i) out[i] = clamp_code(fmaf(x[i], C1, C2));
 }
 
+/* The fused kernel's form of the ExpCast encode, for counting how often it
+ * differs from the reference's: u = fmaf(s, a, b) in units of 2^-24 (s the
+ * raw FP32 logit q8 . k8, a and b the per-row slope and offset the kernel
+ * derived from the scales and the running max), code = RNE(u * 2^24) with
+ * negatives at 0 (the kernel's cvt.rn.relu to the f16 subnormal grid).  No
+ * upper clamp: the kernel shifts b so that the row's largest code is <= 120. */
+void vco_fused_codes(const float* s, const float* a, const float* b, int64_t n, uint8_t* out) {
+    for (int64_t i = 0; i < n; ++i) {
+        const float u = fmaf(s[i], a[i], b[i]) * 16777216.0f;
+        if (!(u > 0.0f)) { out[i] = 0; continue; }
+        const float r = rintf(u);
+        out[i] = (uint8_t)(r > 255.0f ? 255.0f : r);
+    }
+}
+
 /* ExpCast exactly as core.py:67-68 evaluates it: widened product and sum in
  * FP64, one cast to FP32, torch.round (RNE), clamp. */
 void vco_expcast_fp64(const float* x, uint8_t* out, int64_t n) {

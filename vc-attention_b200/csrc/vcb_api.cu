@@ -96,6 +96,24 @@ int check_qk(const vcb_qk_args* a, bool quantise) {
     return VCB_OK;
 }
 
+int check_attn(const vcb_attn_args* a) {
+    VCB_REQUIRE(a, "null argument struct");
+    VCB_REQUIRE(a->q8 && a->k8 && a->v8 && a->q_scale && a->k_scale && a->v_meta && a->out,
+                "operands must be non-null");
+    VCB_REQUIRE(a->heads > 0 && a->sq > 0 && a->sk > 0 && a->heads < 65536, "invalid sizes");
+    VCB_REQUIRE(a->sq < (1ll << 31) && a->sk < (1ll << 31), "sequence too long");
+    VCB_REQUIRE(a->dv >= 1 && a->dv <= 128, "value dimension must be in [1, 128]");
+    VCB_REQUIRE(a->kv_block == 128, "kv_block must be 128");
+    VCB_REQUIRE(a->q_block >= 1 && a->q_block <= 4096, "q_block must be in [1, 4096]");
+    VCB_REQUIRE(a->k_quant_block >= 128 && a->k_quant_block <= 4096 && a->k_quant_block % 128 == 0,
+                "k_quant_block must be a multiple of kv_block (128), at most 4096");
+    VCB_REQUIRE(a->scale > 0.0f && a->scale <= 3.4e38f, "scale must be positive and finite");
+    VCB_REQUIRE(a->out_dtype >= VCB_F32 && a->out_dtype <= VCB_BF16, "unknown output dtype");
+    VCB_REQUIRE(aligned16(a->q8) && aligned16(a->k8) && aligned16(a->v8) && aligned16(a->v_meta),
+                "operands must be 16-byte aligned");
+    return VCB_OK;
+}
+
 }  // namespace
 }  // namespace vcb
 
@@ -206,24 +224,28 @@ int vcb_prepare_v(const vcb_v_args* a, void* stream) {
     return vprep_run(a, static_cast<cudaStream_t>(stream));
 }
 
-int vcb_attention_fp8(const vcb_attn_args* a, void* stream) {
-    VCB_REQUIRE(a, "null argument struct");
-    VCB_REQUIRE(a->q8 && a->k8 && a->v8 && a->q_scale && a->k_scale && a->v_meta && a->out,
-                "operands must be non-null");
-    VCB_REQUIRE(a->heads > 0 && a->sq > 0 && a->sk > 0 && a->heads < 65536, "invalid sizes");
-    VCB_REQUIRE(a->sq < (1ll << 31) && a->sk < (1ll << 31), "sequence too long");
-    VCB_REQUIRE(a->dv >= 1 && a->dv <= 128, "value dimension must be in [1, 128]");
-    VCB_REQUIRE(a->kv_block == 128, "kv_block must be 128");
-    VCB_REQUIRE(a->q_block >= 1 && a->q_block <= 4096, "q_block must be in [1, 4096]");
-    VCB_REQUIRE(a->k_quant_block >= 128 && a->k_quant_block <= 4096 && a->k_quant_block % 128 == 0,
-                "k_quant_block must be a multiple of kv_block (128), at most 4096");
-    VCB_REQUIRE(a->scale > 0.0f && a->scale <= 3.4e38f, "scale must be positive and finite");
-    VCB_REQUIRE(a->out_dtype >= VCB_F32 && a->out_dtype <= VCB_BF16, "unknown output dtype");
-    VCB_REQUIRE(aligned16(a->q8) && aligned16(a->k8) && aligned16(a->v8) && aligned16(a->v_meta),
-                "operands must be 16-byte aligned");
-    int rc = require_sm100(nullptr);
+int vcb_attention_fp8_probe(const vcb_attn_args* a, const vcb_attn_probe* pr, void* stream) {
+    VCB_REQUIRE(pr, "null probe struct");
+    VCB_REQUIRE(pr->logits && pr->codes && pr->rowstat, "probe buffers must be non-null");
+    int rc = check_attn(a);
     if (rc) return rc;
-    return attn_run(a, static_cast<cudaStream_t>(stream));
+    VCB_REQUIRE(pr->head >= 0 && pr->head < a->heads, "probe head out of range");
+    VCB_REQUIRE(pr->q_tile >= 0 && pr->q_tile < (a->sq + 127) / 128, "probe query tile out of range");
+    VCB_REQUIRE(pr->tile_begin >= 0 && pr->tile_count >= 1 &&
+                    (int64_t)pr->tile_begin + pr->tile_count <= (a->sk + 127) / 128,
+                "probe KV tiles out of range");
+    VCB_REQUIRE((reinterpret_cast<uintptr_t>(pr->codes) & 3u) == 0, "probe codes must be 4-byte aligned");
+    rc = require_sm100(nullptr);
+    if (rc) return rc;
+    return attn_run(a, pr, static_cast<cudaStream_t>(stream));
+}
+
+int vcb_attention_fp8(const vcb_attn_args* a, void* stream) {
+    int rc = check_attn(a);
+    if (rc) return rc;
+    rc = require_sm100(nullptr);
+    if (rc) return rc;
+    return attn_run(a, nullptr, static_cast<cudaStream_t>(stream));
 }
 
 // Workspace of vcb_forward, carved in this order (256-byte aligned pieces):
@@ -306,7 +328,7 @@ int vcb_forward(const vcb_forward_args* a, void* stream) {
     if (rc) return rc;
     rc = vprep_run(&va, st);
     if (rc) return rc;
-    return attn_run(&at, st);
+    return attn_run(&at, nullptr, st);
 }
 
 int vcb_wait_selftest(int complete, const void* src, int32_t* status, int32_t* report, void* stream) {
@@ -317,11 +339,15 @@ int vcb_wait_selftest(int complete, const void* src, int32_t* status, int32_t* r
     return wait_selftest_run(complete, src, status, report, static_cast<cudaStream_t>(stream));
 }
 
+// The copy is ordered on the caller's stream only (no legacy default stream,
+// no device-wide synchronisation); the host then waits for that stream.
 int vcb_read_status(const int32_t* status, void* stream, int32_t* flags) {
     VCB_REQUIRE(status && flags, "status and flags must be non-null");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int32_t word = 0;
+    VCB_CUDA(cudaMemcpyAsync(&word, status, sizeof(int32_t), cudaMemcpyDeviceToHost, st));
     VCB_CUDA(cudaStreamSynchronize(st));
-    VCB_CUDA(cudaMemcpy(flags, status, sizeof(int32_t), cudaMemcpyDeviceToHost));
+    *flags = word;
     return VCB_OK;
 }
 

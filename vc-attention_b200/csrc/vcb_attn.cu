@@ -69,6 +69,7 @@ constexpr float kC1 = 11.541560173034668f;       // 8 log2(e) in fp32
 constexpr float kC2 = 119.6500015258789f;        // 119.65 in fp32
 constexpr float kTwoM24 = 5.9604644775390625e-08f;   // 2^-24
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kMinNormal = 1.17549435e-38f;    // 2^-126
 
 struct Params {
     CUtensorMap tm_q, tm_k, tm_v;
@@ -81,6 +82,11 @@ struct Params {
     int dv, q_block, kq, nqb, nkb, T;
     int out_dtype;
     float scale;
+    // diagnostic dump of one CTA's softmax (vcb_attention_fp8_probe)
+    float* pr_logits;      // [pr_count][128][128] raw accumulators q8 . k8 (masked keys -inf)
+    uint8_t* pr_codes;     // [pr_count][128][128] P bytes as stored for the PV MMA
+    float* pr_rowstat;     // [pr_count][128][4]: running max after the tile, A, B, alpha
+    int pr_head, pr_qtile, pr_begin, pr_count;
 };
 
 struct Bars {
@@ -293,7 +299,7 @@ __device__ __forceinline__ void tmem_st16x2_16(uint32_t taddr, const uint32_t (&
         : "memory");
 }
 
-template <bool EXPCAST>
+template <bool EXPCAST, bool PROBE>
 __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, volatile int* abort, uint32_t tmem,
                              int qtile, int head, int quarter, int sub, int lane) {
     // warp (quarter, sub) owns rows quarter*32 + sub*16 + [0, 16); lanes t and
@@ -351,15 +357,19 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, vola
         // when the maximum did not move (the correction skips its rescale then)
         const float alpha = ex2_ftz(__fmul_rn(m - m_new, kLog2e));
         float A, Bc;
+        // A is kept at or above the smallest normal float: a masked key (-inf)
+        // times A must stay -inf (code 0, no mass), never -inf * 0 = NaN.  When
+        // c underflows that far, every logit s * c is below 2^-100 and the
+        // codes come out as for A = 0, as in the reference.
         if (EXPCAST) {
             // in units of 2^-24 throughout: scaling by a power of two is exact,
             // so this is the unscaled computation times 2^-24, bit for bit
-            A = __fmul_rn(c, kC1 * kTwoM24);
+            A = fmaxf(__fmul_rn(c, kC1 * kTwoM24), kMinNormal);
             Bc = __fsub_rn(kC2 * kTwoM24, __fmul_rn(m_new, kC1 * kTwoM24));
             const float umax = fmaf(rmax, A, Bc);
             if (umax > 120.25f * kTwoM24) Bc = __fsub_rn(Bc, __fsub_rn(umax, kC2 * kTwoM24));
         } else {
-            A = __fmul_rn(c, kLog2e);
+            A = fmaxf(__fmul_rn(c, kLog2e), kMinNormal);
             Bc = __fsub_rn(8.0f, __fmul_rn(m_new, kLog2e));
         }
         const float2 AA = make_float2(A, A), BB = make_float2(Bc, Bc);
@@ -390,6 +400,19 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, vola
         // ms already holds sum(p * 256).
         float M = __fadd_rn(__fadd_rn(ms[0], ms[1]), __fadd_rn(ms[2], ms[3]));
         if (EXPCAST) M = __fmul_rn(M, 256.0f);
+        if (PROBE && head == p.pr_head && qtile == p.pr_qtile && j >= p.pr_begin && j < p.pr_begin + p.pr_count) {
+            const int64_t t = j - p.pr_begin;
+            float* lg = p.pr_logits + (t * 128 + row) * 128 + hs * 64;
+            uint32_t* cd = reinterpret_cast<uint32_t*>(p.pr_codes + (t * 128 + row) * 128 + hs * 64);
+#pragma unroll
+            for (int i = 0; i < 64; ++i) lg[i] = __uint_as_float(r[i]);
+#pragma unroll
+            for (int w = 0; w < 16; ++w) cd[w] = pk[w];
+            if (hs == 0) {
+                float* rs = p.pr_rowstat + (t * 128 + row) * 4;
+                rs[0] = m_new; rs[1] = A; rs[2] = Bc; rs[3] = alpha;
+            }
+        }
         // P_j over this thread's own (already read) S_j columns: 4 codes per
         // 32-bit column, the A-operand layout of the PV MMA
         tmem_st16x2_16(ts, pk);
@@ -500,7 +523,7 @@ __device__ void correction_role(const Params& p, uint8_t* smem, const Bars& B, v
     }
 }
 
-template <bool EXPCAST, bool HAS_MEAN>
+template <bool EXPCAST, bool HAS_MEAN, bool PROBE>
 __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant__ Params p) {
     // The swizzled TMA/MMA layouts need a 1024-byte aligned base; the kernel
     // declares no static shared memory, so the dynamic window starts aligned.
@@ -555,7 +578,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
         if (warp == 1 && lane == 0) mma_issuer(p, smem, B, abort, tmem);
         if (warp == 2 && lane == 0) meta_producer(p, smem, B, abort, head);
     } else if (warp < 12) {
-        softmax_role<EXPCAST>(p, smem, B, abort, tmem, qtile, head, warp & 3, (warp - 4) >> 2, lane);
+        softmax_role<EXPCAST, PROBE>(p, smem, B, abort, tmem, qtile, head, warp & 3, (warp - 4) >> 2, lane);
     } else {
         reg_alloc<112>();
         correction_role<HAS_MEAN>(p, smem, B, abort, tmem, qtile, head, warp & 3, (warp - 12) >> 2, lane);
@@ -603,10 +626,11 @@ int make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t planes)
     return VCB_OK;
 }
 
-template <bool E, bool M>
+template <bool E, bool M, bool P>
 int launch(const Params& p, dim3 grid, cudaStream_t st) {
-    VCB_CUDA(cudaFuncSetAttribute(attn_kernel<E, M>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemAlloc));
-    attn_kernel<E, M><<<grid, kThreads, kSmemAlloc, st>>>(p);
+    VCB_CUDA(cudaFuncSetAttribute(attn_kernel<E, M, P>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)kSmemAlloc));
+    attn_kernel<E, M, P><<<grid, kThreads, kSmemAlloc, st>>>(p);
     VCB_CUDA(cudaGetLastError());
     return VCB_OK;
 }
@@ -670,7 +694,7 @@ __global__ void __launch_bounds__(128, 1)
 
 }  // namespace
 
-int attn_run(const vcb_attn_args* a, cudaStream_t st) {
+int attn_run(const vcb_attn_args* a, const vcb_attn_probe* probe, cudaStream_t st) {
     Params p;
     memset(&p, 0, sizeof(p));
     const int64_t sq_pad = vcb_padded_rows(a->sq, a->q_block);
@@ -696,8 +720,21 @@ int attn_run(const vcb_attn_args* a, cudaStream_t st) {
     p.out_dtype = a->out_dtype;
     p.scale = a->scale;
     const dim3 grid((unsigned)((a->sq + kBM - 1) / kBM), (unsigned)a->heads);
-    if (a->expcast) return a->has_mean ? launch<true, true>(p, grid, st) : launch<true, false>(p, grid, st);
-    return a->has_mean ? launch<false, true>(p, grid, st) : launch<false, false>(p, grid, st);
+    if (probe) {
+        p.pr_logits = probe->logits;
+        p.pr_codes = probe->codes;
+        p.pr_rowstat = probe->rowstat;
+        p.pr_head = (int)probe->head;
+        p.pr_qtile = (int)probe->q_tile;
+        p.pr_begin = probe->tile_begin;
+        p.pr_count = probe->tile_count;
+        if (a->expcast)
+            return a->has_mean ? launch<true, true, true>(p, grid, st) : launch<true, false, true>(p, grid, st);
+        return a->has_mean ? launch<false, true, true>(p, grid, st) : launch<false, false, true>(p, grid, st);
+    }
+    if (a->expcast)
+        return a->has_mean ? launch<true, true, false>(p, grid, st) : launch<true, false, false>(p, grid, st);
+    return a->has_mean ? launch<false, true, false>(p, grid, st) : launch<false, false, false>(p, grid, st);
 }
 
 int wait_selftest_run(int complete, const void* src, int32_t* status, int32_t* report, cudaStream_t st) {

@@ -22,6 +22,11 @@
 // The device address of the array is looked up with cudaGetSymbolAddress the
 // first time the entry point runs on a device, with that device current; that
 // first call on each device should therefore come before any stream capture.
+// The address is remembered together with the identity of the CUDA context it
+// was looked up in.  If the process resets the device (cudaDeviceReset) and a
+// new context loads the library's module again, possibly at another address,
+// the next call sees a different context and looks the address up again
+// instead of handing the kernels a stale pointer.
 #include <mutex>
 
 #include "vcb_internal.h"
@@ -34,22 +39,62 @@ constexpr size_t kScratchBytes = size_t(8) << 20;
 static __device__ __align__(256) unsigned char g_qk_scratch[kScratchBytes];
 
 constexpr int kMaxDevices = 64;
-void* g_scratch_ptr[kMaxDevices] = {};
+struct ScratchEntry {
+    void* ptr;
+    unsigned long long ctx_id;     // identity of the context the address belongs to
+};
+ScratchEntry g_scratch[kMaxDevices] = {};
 std::mutex g_scratch_mutex;
 
-// Device address of g_qk_scratch on the current device (looked up once).
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
+
+// Process-unique identity of the current CUDA context (cuCtxGetId, CUDA 12.0);
+// 0 when the thread has no current context yet.
+int current_context_id(unsigned long long* id) {
+    static CtxGetCurrentFn get_current = nullptr;
+    static CtxGetIdFn get_id = nullptr;
+    if (!get_current || !get_id) {
+        void* a = nullptr;
+        void* b = nullptr;
+        cudaDriverEntryPointQueryResult qa, qb;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &a, cudaEnableDefault, &qa) != cudaSuccess ||
+            qa != cudaDriverEntryPointSuccess || !a ||
+            cudaGetDriverEntryPoint("cuCtxGetId", &b, cudaEnableDefault, &qb) != cudaSuccess ||
+            qb != cudaDriverEntryPointSuccess || !b)
+            return fail(VCB_ERR_CUDA, "cuCtxGetCurrent / cuCtxGetId are not available from the driver");
+        get_current = reinterpret_cast<CtxGetCurrentFn>(a);
+        get_id = reinterpret_cast<CtxGetIdFn>(b);
+    }
+    CUcontext ctx = nullptr;
+    *id = 0;
+    if (get_current(&ctx) != CUDA_SUCCESS) return fail(VCB_ERR_CUDA, "cuCtxGetCurrent failed");
+    if (ctx && get_id(ctx, id) != CUDA_SUCCESS) return fail(VCB_ERR_CUDA, "cuCtxGetId failed");
+    return VCB_OK;
+}
+
+// Device address of g_qk_scratch on the current device, looked up once per
+// device and context (cudaGetSymbolAddress also makes the device's primary
+// context current when the thread has none yet).
 int scratch_address(void** out) {
     int dev = 0;
     VCB_CUDA(cudaGetDevice(&dev));
     if (dev < 0 || dev >= kMaxDevices) return fail(VCB_ERR_INVALID_ARGUMENT, "device ordinal %d out of range", dev);
+    unsigned long long ctx = 0;
+    int rc = current_context_id(&ctx);
+    if (rc) return rc;
     std::lock_guard<std::mutex> lock(g_scratch_mutex);
-    if (!g_scratch_ptr[dev]) {
+    ScratchEntry& e = g_scratch[dev];
+    if (!e.ptr || ctx == 0 || e.ctx_id != ctx) {
         void* p = nullptr;
-        cudaError_t e = cudaGetSymbolAddress(&p, g_qk_scratch);
-        if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_qk_scratch)");
-        g_scratch_ptr[dev] = p;
+        cudaError_t err = cudaGetSymbolAddress(&p, g_qk_scratch);
+        if (err != cudaSuccess) return cuda_fail(err, "cudaGetSymbolAddress(g_qk_scratch)");
+        rc = current_context_id(&ctx);
+        if (rc) return rc;
+        e.ptr = p;
+        e.ctx_id = ctx;
     }
-    *out = g_scratch_ptr[dev];
+    *out = e.ptr;
     return VCB_OK;
 }
 

@@ -4,6 +4,6 @@ Same public surface as czfsdg/vc-attention's ``vc_attention`` package
 (``Config``, ``LayoutCache``, ``attention``; src/vc_attention/__init__.py:3-5).
 """
 from .core import Config, LayoutCache, attention
-from .streamed import attention_streamed
+from .streamed import attention_streamed, check_streamed
 
-__all__ = ["Config", "LayoutCache", "attention", "attention_streamed"]
+__all__ = ["Config", "LayoutCache", "attention", "attention_streamed", "check_streamed"]

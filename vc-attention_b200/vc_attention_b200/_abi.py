@@ -56,6 +56,11 @@ class AttnArgs(ctypes.Structure):
                 ("out_dtype", c_int), ("status", c_void_p)]
 
 
+class AttnProbe(ctypes.Structure):
+    _fields_ = [("head", c_int64), ("q_tile", c_int64), ("tile_begin", c_int), ("tile_count", c_int),
+                ("logits", c_void_p), ("codes", c_void_p), ("rowstat", c_void_p)]
+
+
 class ForwardArgs(ctypes.Structure):
     _fields_ = [("q", c_void_p), ("k", c_void_p), ("v", c_void_p), ("dtype", c_int), ("heads", c_int64),
                 ("sq", c_int64), ("sk", c_int64), ("d", c_int), ("dv", c_int), ("pi", c_void_p),
@@ -82,6 +87,7 @@ SIGNATURES = {
     "vcb_group_values": (c_int, [ctypes.POINTER(GroupArgs), c_void_p]),
     "vcb_prepare_v": (c_int, [ctypes.POINTER(VArgs), c_void_p]),
     "vcb_attention_fp8": (c_int, [ctypes.POINTER(AttnArgs), c_void_p]),
+    "vcb_attention_fp8_probe": (c_int, [ctypes.POINTER(AttnArgs), ctypes.POINTER(AttnProbe), c_void_p]),
     "vcb_forward_workspace": (c_size_t, [ctypes.POINTER(ForwardArgs)]),
     "vcb_forward": (c_int, [ctypes.POINTER(ForwardArgs), c_void_p]),
     "vcb_read_status": (c_int, [c_void_p, c_void_p, ctypes.POINTER(ctypes.c_int32)]),

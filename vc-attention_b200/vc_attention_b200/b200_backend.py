@@ -184,6 +184,8 @@ def _attention(q, k, v, cfg, *, cache, step, total_steps, request_id, layer_id, 
         request_id = "one-shot" if request_id is None else request_id
     elif cache.config != cfg:
         raise ValueError("cache.config must match config")
+    if status is not None and (status.device != q.device or status.dtype != torch.int32 or status.numel() != 1):
+        raise ValueError("status must be a one-element int32 tensor on the inputs' device")
     snapshot = cache._snapshot(layer_id)
     with torch.cuda.device(q.device):
         pi, active, refreshed = cache.layout(v, step=step, total_steps=total_steps, request_id=request_id,
@@ -192,10 +194,11 @@ def _attention(q, k, v, cfg, *, cache, step, total_steps, request_id, layer_id, 
         try:
             output = forward(qc, kc, vc, cfg, pi=pi, active=active, scale=scale, status=status,
                              check_status=status is None)
-        except ValueError:
+        except (ValueError, RuntimeError):
             cache._restore(snapshot, layer_id)
             raise
-    return output, {
+    extra = {} if status is None else {"rollback": lambda: cache._restore(snapshot, layer_id)}
+    return output, {**extra,
         "backend": "b200_fp8",
         "smoothing_active": active,
         "layout_refreshed": refreshed,

@@ -183,12 +183,24 @@ def attention(
     scale=None,
     causal=False,
     mask=None,
+    status=None,
 ):
-    """Return (output, counters) as core.attention does (core.py:243-351)."""
+    """Return (output, counters) as core.attention does (core.py:243-351).
+
+    ``status`` (an addition to the reference's signature, default None) is
+    for callers that read the device status once per step instead of once
+    per call.  By default the call waits for the current stream, reads the
+    status word the kernels write, and raises ValueError for non-finite
+    Q/K/V (as the reference's isfinite check does) or RuntimeError for an
+    expired device wait.  Given a caller-owned zeroed int32 CUDA tensor of
+    one element, the call only queues the work and ORs its flags into that
+    word; the caller later calls ``b200_backend.raise_for_status(status)``
+    and, if it raises, ``counters["rollback"]()`` to put the layout cache
+    back as it was before this call."""
     cfg = config or Config()
     _validate(q, k, v, causal, mask)
     from .b200_backend import _attention
 
     return _attention(q, k, v, cfg, cache=cache, step=step, total_steps=total_steps,
                       request_id=request_id, layer_id=layer_id,
-                      scale=q.shape[-1] ** -0.5 if scale is None else scale)
+                      scale=q.shape[-1] ** -0.5 if scale is None else scale, status=status)

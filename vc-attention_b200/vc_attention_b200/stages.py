@@ -56,16 +56,46 @@ def prepare_v(v, *, pi=None, active=True, mean_dtype="float16", kv_block=128, st
     return v8, meta
 
 
+def _attn_args(q8, qs, k8, ks, v8, meta, out, *, heads, sq, sk, dv, q_block, k_quant_block, expcast, has_mean,
+               scale, status):
+    return _abi.AttnArgs(q8=q8.data_ptr(), q_scale=qs.data_ptr(), k8=k8.data_ptr(), k_scale=ks.data_ptr(),
+                         v8=v8.data_ptr(), v_meta=meta.data_ptr(), heads=heads, sq=sq, sk=sk, dv=dv,
+                         q_block=q_block, k_quant_block=k_quant_block, kv_block=128, expcast=int(expcast),
+                         has_mean=int(has_mean), scale=float(scale), out=out.data_ptr(),
+                         out_dtype=_DTYPES[out.dtype], status=_i(status))
+
+
 def attention_fp8(q8, qs, k8, ks, v8, meta, *, heads, sq, sk, dv, q_block=128, k_quant_block=256, expcast=True,
                   has_mean=True, scale, out_dtype=torch.bfloat16, out=None, status=None):
     """vcb_attention_fp8 on prepared operands; returns [heads, sq, dv]."""
     lib = _extension()
     if out is None:
         out = torch.empty((heads, sq, dv), dtype=out_dtype, device=q8.device)
-    a = _abi.AttnArgs(q8=q8.data_ptr(), q_scale=qs.data_ptr(), k8=k8.data_ptr(), k_scale=ks.data_ptr(),
-                      v8=v8.data_ptr(), v_meta=meta.data_ptr(), heads=heads, sq=sq, sk=sk, dv=dv, q_block=q_block,
-                      k_quant_block=k_quant_block, kv_block=128, expcast=int(expcast), has_mean=int(has_mean),
-                      scale=float(scale), out=out.data_ptr(), out_dtype=_DTYPES[out.dtype], status=_i(status))
+    a = _attn_args(q8, qs, k8, ks, v8, meta, out, heads=heads, sq=sq, sk=sk, dv=dv, q_block=q_block,
+                   k_quant_block=k_quant_block, expcast=expcast, has_mean=has_mean, scale=scale, status=status)
     with torch.cuda.device(q8.device):
         _abi.check(lib, lib.vcb_attention_fp8(ctypes.byref(a), _stream(q8.device)))
     return out
+
+
+def attention_fp8_probe(q8, qs, k8, ks, v8, meta, *, heads, sq, sk, dv, head, q_tile, tile_begin=0,
+                        tile_count=None, q_block=128, k_quant_block=256, expcast=True, has_mean=True, scale,
+                        out_dtype=torch.bfloat16, status=None):
+    """vcb_attention_fp8_probe: the full attention plus a dump of one CTA's
+    softmax.  Returns (out, logits [n, 128, 128] f32, codes [n, 128, 128] u8,
+    rowstat [n, 128, 4] f32 = running max, slope A, offset B, alpha) for KV
+    tiles [tile_begin, tile_begin + n) of (head, q_tile)."""
+    lib = _extension()
+    dev = q8.device
+    n = -(-sk // 128) - tile_begin if tile_count is None else tile_count
+    out = torch.empty((heads, sq, dv), dtype=out_dtype, device=dev)
+    logits = torch.empty((n, 128, 128), dtype=torch.float32, device=dev)
+    codes = torch.empty((n, 128, 128), dtype=torch.uint8, device=dev)
+    rowstat = torch.empty((n, 128, 4), dtype=torch.float32, device=dev)
+    a = _attn_args(q8, qs, k8, ks, v8, meta, out, heads=heads, sq=sq, sk=sk, dv=dv, q_block=q_block,
+                   k_quant_block=k_quant_block, expcast=expcast, has_mean=has_mean, scale=scale, status=status)
+    pr = _abi.AttnProbe(head=head, q_tile=q_tile, tile_begin=tile_begin, tile_count=n, logits=logits.data_ptr(),
+                        codes=codes.data_ptr(), rowstat=rowstat.data_ptr())
+    with torch.cuda.device(dev):
+        _abi.check(lib, lib.vcb_attention_fp8_probe(ctypes.byref(a), ctypes.byref(pr), _stream(dev)))
+    return out, logits, codes, rowstat

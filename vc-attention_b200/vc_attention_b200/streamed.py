@@ -63,12 +63,17 @@ def attention_streamed(q, k, v, config=None, *, cache=None, step=0, total_steps=
     at a time (default: a fortieth of them, at least one).  With
     ``synchronize=False`` the call returns once the work is queued (the
     output is complete when the device's current stream reaches this point)
-    and skips the check for non-finite inputs."""
+    and does not read the device status word.  The caller then owns that
+    check: ``stats["status"]`` is the status word (device int32) and
+    ``check_streamed(stats)`` reads it once the stream has reached it,
+    raises what ``attention`` raises (ValueError for non-finite inputs,
+    RuntimeError for an expired device wait or a failed layout check) and,
+    on any raise, rolls the layout cache back to its state before the call."""
     cfg = config or Config()
     _validate(q, k, v, False, None)
     if q.device.type != "cpu":
         raise ValueError("attention_streamed takes host tensors; use attention for device tensors")
-    from .b200_backend import _attention, raise_for_status
+    from .b200_backend import _attention
 
     device = torch.device(device if device is not None else "cuda")
     b, h, sq, d = q.shape
@@ -133,14 +138,28 @@ def attention_streamed(q, k, v, config=None, *, cache=None, step=0, total_steps=
             main.wait_stream(c)
         main.wait_stream(d2h)
         main.wait_stream(h2d)
+
+        def rollback():
+            cache._request_id, states, fields = saved
+            cache._states = states
+            for key, val in states.items():
+                val.clear()
+                val.update(fields[key])
+
+        stats = dict(stats, streamed_chunks=len(parts), status=status, rollback=rollback)
         if synchronize:
-            try:
-                raise_for_status(status)
-            except ValueError:
-                cache._request_id, states, fields = saved
-                cache._states = states
-                for key, val in states.items():
-                    val.clear()
-                    val.update(fields[key])
-                raise
-    return out, dict(stats, streamed_chunks=len(parts))
+            check_streamed(stats)
+    return out, stats
+
+
+def check_streamed(stats):
+    """Reads the status word of an ``attention_streamed`` call (waiting for
+    the device's current stream) and raises what ``attention`` raises, after
+    rolling the layout cache back to its state before that call."""
+    from .b200_backend import raise_for_status
+
+    try:
+        raise_for_status(stats["status"])
+    except (ValueError, RuntimeError):
+        stats["rollback"]()
+        raise

@@ -222,7 +222,7 @@ def rows_check(q, k, v, out, cfg, *, head, r0, pi, active, scale=D ** -0.5):
     ph = None if pi is None else pi[:, hs].contiguous()
     q8, qs, k8, ks = stages.quantize_qk(qh, kh, pi=ph, q_block=cfg.q_block, k_quant_block=cfg.k_quant_block,
                                         k_smooth=cfg.k_smooth, hadamard=cfg.qk_hadamard)
-    v8, meta = stages.prepare_v(vh, pi=ph, active=active, mean_dtype=cfg.mean_dtype)
+    v8, meta, _ = stages.prepare_v(vh, pi=ph, active=active, mean_dtype=cfg.mean_dtype)
     sk, dv = k.shape[2], v.shape[3]
     rows = torch.arange(r0, r0 + 128, device=q.device)
     keys = torch.arange(sk, device=q.device)
@@ -404,11 +404,12 @@ def run_ours(args, world, rank, local):
     # dominant kernel alone: the fused attention on prepared operands
     pi, _ = group_values(v, clusters=8, iterations=2)
     q8, qs, k8, ks = stages.quantize_qk(q, k, pi=pi)
-    v8, meta = stages.prepare_v(v, pi=pi, active=True)
+    v8, meta, mop = stages.prepare_v(v, pi=pi, active=True)
     attn_out = torch.empty((h_loc, S, D), dtype=torch.bfloat16, device=device)
 
     def attn():
-        stages.attention_fp8(q8, qs, k8, ks, v8, meta, heads=h_loc, sq=S, sk=S, dv=D, expcast=True, has_mean=True,
+        stages.attention_fp8(q8, qs, k8, ks, v8, meta, mean_op=mop, heads=h_loc, sq=S, sk=S, dv=D, expcast=True,
+                             has_mean=True,
                              scale=scale, out=attn_out)
 
     for _ in range(3):
@@ -577,14 +578,14 @@ def run_case(args):
         print(json.dumps({"case": "prep", "heads": args.heads, "steps": args.steps}))
         return
     q8, qs, k8, ks = stages.quantize_qk(q, k)
-    v8, meta = stages.prepare_v(v, active=True)
+    v8, meta, mop = stages.prepare_v(v, active=True)
     del q, k, v
     out = torch.empty((args.heads, S, D), dtype=torch.bfloat16, device="cuda")
     times = []
     for _ in range(args.steps):
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
-        stages.attention_fp8(q8, qs, k8, ks, v8, meta, heads=args.heads, sq=S, sk=S, dv=D, expcast=True,
+        stages.attention_fp8(q8, qs, k8, ks, v8, meta, mean_op=mop, heads=args.heads, sq=S, sk=S, dv=D, expcast=True,
                              has_mean=True, scale=D ** -0.5, out=out)
         e.record()
         e.synchronize()

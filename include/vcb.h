@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define VCB_ABI_VERSION 1
+#define VCB_ABI_VERSION 2
 #define VCB_NUMERICAL_CONTRACT_VERSION 2   /* bindings.cpp:232 */
 
 enum vcb_status {
@@ -144,6 +144,10 @@ typedef struct {
     int kv_block;           /* 128 */
     uint8_t* v8;            /* [heads, T, 128 channels, kv_block tokens] e4m3 residual */
     float* v_meta;          /* [heads, T, 2, 128]: vscale, then mu/vscale at mean_type */
+    uint16_t* v_mean_op;    /* [heads, T, 128, 16] bf16, written when active (nullable): per channel the
+                               stored mean mu/vscale as bf16 pieces u1 + u2 + u3 (u1 truncated, u2 and u3
+                               rounded remainders) in the row [u1, u2, u3, u1, u2, u1, 0 x 10], the B
+                               operand of the attention kernel's row-mass x mean MMA */
     int32_t* status;        /* device status word (nullable) */
 } vcb_v_args;
 
@@ -156,6 +160,7 @@ typedef struct {
     const uint8_t* q8; const float* q_scale;
     const uint8_t* k8; const float* k_scale;
     const uint8_t* v8; const float* v_meta;
+    const uint16_t* v_mean_op;  /* vcb_v_args.v_mean_op; required when has_mean */
     int64_t heads, sq, sk;
     int dv;
     int q_block, k_quant_block, kv_block;

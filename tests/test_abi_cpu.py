@@ -23,7 +23,7 @@ def test_library_exports_every_declared_symbol():
     lib = _abi.load()
     for name in declared_symbols():
         assert hasattr(lib, name), name
-    assert lib.vcb_abi_version() == 1
+    assert lib.vcb_abi_version() == 2
     assert lib.vcb_numerical_contract_version() == 2
     import json
     info = json.loads(lib.vcb_build_info().decode())

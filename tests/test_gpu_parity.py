@@ -133,13 +133,28 @@ def test_prepare_v_bit_exact(mean_dtype, active, perm, dtype, s, dv):
     h = 2
     v = (torch.randn(1, h, s, dv, generator=g) * 0.3 + torch.randn(1, h, 1, dv, generator=g) * 3).to(dtype)
     pi = torch.stack([torch.randperm(s, generator=g) for _ in range(h)]).int().view(1, h, s) if perm else None
-    v8, meta = stages.prepare_v(v.cuda(), pi=None if pi is None else pi.cuda(), active=active, mean_dtype=mean_dtype)
+    v8, meta, mop = stages.prepare_v(v.cuda(), pi=None if pi is None else pi.cuda(), active=active, mean_dtype=mean_dtype)
     r8, rvs, rmu = O.value_tiles(_flat_np(v), None if pi is None else pi.view(h, s).numpy(), active=active,
                                  mean_dtype=mean_dtype, kv_block=128)
     meta = meta.cpu().numpy()
     assert np.array_equal(meta[:, :, 0], rvs)
     assert np.array_equal(meta[:, :, 1], rmu)
     assert np.array_equal(v8.cpu().numpy(), r8)
+    if active:
+        # the mean operand of the row-mass x mean MMA: the stored mean as bf16
+        # pieces u1 (truncated) + u2 + u3 (rounded remainders), which add up to
+        # it exactly, in the row [u1, u2, u3, u1, u2, u1, 0 ...]
+        stored = torch.from_numpy(rmu)
+        u1 = (stored.view(torch.int32) & -65536).view(torch.float32)
+        u2 = (stored - u1).to(torch.bfloat16).float()
+        u3 = (stored - u1 - u2).to(torch.bfloat16).float()
+        assert torch.equal(u1 + u2 + u3, stored)
+        want = torch.zeros(*stored.shape, 16, dtype=torch.bfloat16)
+        for slot, piece in enumerate((u1, u2, u3, u1, u2, u1)):
+            want[..., slot] = piece.to(torch.bfloat16)
+        assert torch.equal(mop.cpu(), want.view(torch.int16))
+    else:
+        assert mop is None
 
 
 def test_prepare_v_reference_tiles(golden):
@@ -147,7 +162,7 @@ def test_prepare_v_reference_tiles(golden):
     from vc_attention_b200 import stages
     tile = cases.exact_value_tile()          # [1, 2, 128, 21]
     for mean_dtype in ("float16", "bfloat16", "float32"):
-        v8, meta = stages.prepare_v(tile.cuda(), active=True, mean_dtype=mean_dtype)
+        v8, meta, _ = stages.prepare_v(tile.cuda(), active=True, mean_dtype=mean_dtype)
         payload = v8.cpu().numpy()[:, 0, :21, :].transpose(0, 2, 1)
         assert np.array_equal(payload, golden[f"vtile_exact_{mean_dtype}_payload"][0])
         assert np.array_equal(meta.cpu().numpy()[:, 0, 0, :21], golden[f"vtile_exact_{mean_dtype}_scale"][0, :, 0])

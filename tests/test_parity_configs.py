@@ -173,7 +173,7 @@ def _probe(config, seq, seed, *, expcast, q_tile):
     q, k, v = make_qkv(config, seed, device="cuda", heads=1, seq=seq)
     q, k, v = (x.to(torch.bfloat16) for x in (q, k, v))
     q8, qs, k8, ks = stages.quantize_qk(q, k)
-    v8, meta = stages.prepare_v(v, active=False)
+    v8, meta, _ = stages.prepare_v(v, active=False)
     scale = D ** -0.5
     _, logits, codes, rowstat = stages.attention_fp8_probe(
         q8, qs, k8, ks, v8, meta, heads=1, sq=seq, sk=seq, dv=D, head=0, q_tile=q_tile, expcast=expcast,

@@ -249,10 +249,11 @@ int vcb_attention_fp8(const vcb_attn_args* a, void* stream) {
 }
 
 // Workspace of vcb_forward, carved in this order (256-byte aligned pieces):
-// q8, k8, q_scale, k_scale, v8, v_meta, then the Q/K-prep scratch.
+// q8, k8, q_scale, k_scale, v8, v_meta, the V-mean operand, then the Q/K-prep
+// scratch.
 namespace {
 struct ForwardLayout {
-    size_t q8, k8, qs, ks, v8, vm, qk, total;
+    size_t q8, k8, qs, ks, v8, vm, mop, qk, total;
 };
 ForwardLayout forward_layout(const vcb_forward_args* a) {
     auto r = [](size_t b) { return (b + 255) & ~size_t(255); };
@@ -267,6 +268,7 @@ ForwardLayout forward_layout(const vcb_forward_args* a) {
     L.ks = o; o += r((size_t)(a->heads * ((a->sk + a->k_quant_block - 1) / a->k_quant_block)) * 4);
     L.v8 = o; o += r((size_t)(a->heads * T * 128 * 128));
     L.vm = o; o += r((size_t)(a->heads * T * 256) * 4);
+    L.mop = o; o += a->smooth ? r((size_t)(a->heads * T * 128 * 16) * 2) : 0;
     L.qk = o; o += r(qk_workspace_bytes(a->heads, a->sk));
     L.total = o;
     return L;
@@ -313,12 +315,13 @@ int vcb_forward(const vcb_forward_args* a, void* stream) {
     va.v = a->v; va.dtype = a->dtype; va.heads = a->heads; va.s = a->sk; va.dv = a->dv; va.pi = a->pi;
     va.active = a->smooth; va.mean_type = a->mean_type; va.kv_block = a->kv_block;
     va.v8 = reinterpret_cast<uint8_t*>(ws + L.v8); va.v_meta = reinterpret_cast<float*>(ws + L.vm);
+    va.v_mean_op = a->smooth ? reinterpret_cast<uint16_t*>(ws + L.mop) : nullptr;
     va.status = a->status;
     VCB_REQUIRE(a->dv >= 1 && a->dv <= 128, "value dimension must be in [1, 128]");
 
     vcb_attn_args at{};
     at.q8 = qk.q8; at.q_scale = qk.q_scale; at.k8 = qk.k8; at.k_scale = qk.k_scale;
-    at.v8 = va.v8; at.v_meta = va.v_meta; at.heads = a->heads; at.sq = a->sq; at.sk = a->sk; at.dv = a->dv;
+    at.v8 = va.v8; at.v_meta = va.v_meta; at.v_mean_op = va.v_mean_op; at.heads = a->heads; at.sq = a->sq; at.sk = a->sk; at.dv = a->dv;
     at.q_block = a->q_block; at.k_quant_block = a->k_quant_block; at.kv_block = a->kv_block;
     at.expcast = a->expcast; at.has_mean = a->smooth; at.scale = a->scale; at.out = a->out;
     at.out_dtype = a->dtype; at.status = a->status;

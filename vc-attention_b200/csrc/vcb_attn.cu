@@ -1,33 +1,53 @@
-// Fused VC-Attention forward for sm_100a.
+// Fused VC-Attention forward for sm_100a on pairs of SMs.
 //
 // Replaces the reference's host loop over heads x Q tiles x KV tiles
 // (kernels.cu:313-330: a cuBLASLt E4M3 GEMM for S, softmax_update, a second
-// GEMM for PV and accumulate, all through HBM scratch) with one CTA per
-// (head, 128-row Q tile) that keeps every intermediate on chip.
+// GEMM for PV and accumulate, all through HBM scratch) with one persistent
+// kernel that keeps every intermediate on chip.
 //
-// Roles (640 threads, register budgets rebalanced with setmaxnreg):
-//   warp 0      TMA producer: the Q tile once, then K / V tiles into a 4-stage
-//               ring (no cluster multicast).
-//   warp 2      the per-tile V scales and means into a 16-slot ring.
-//   warp 1      MMA issuer (one thread): S_j = Q8 K8_j^T into TMEM
-//               (tcgen05.mma kind::f8f6f4, E4M3 x E4M3 -> F32) and
-//               O_j = P_j R_j with P_j in TMEM and R_j in shared memory.
+// Work decomposition.  Two CTAs form a cluster and share every KV tile: CTA
+// rank r of the pair owns query tile 2p + r of a head (128 rows), and the
+// pair's MMAs are tcgen05.mma.cta_group::2 with M = 256: one instruction,
+// issued by one thread of the even CTA, multiplies both CTAs' rows.  Each CTA
+// loads only its half of every K tile (64 keys), V tile (64 channels) and
+// mean-operand tile, with ordinary (non-multicast) TMA loads that report to
+// the even CTA's barrier.  The grid holds as many pairs as fit on the GPU at
+// once, and each pair walks the (head, pair-of-query-tiles) items
+// c, c + clusters, ... in order, so the K/V of one or two heads are in L2 at
+// a time.  Barrier phases run on across items; the prologue and epilogue of
+// consecutive items overlap.
+//
+// Roles per CTA (640 threads, register budgets rebalanced with setmaxnreg):
+//   warp 0      TMA producer: this CTA's Q tile of each item (2 buffers),
+//               then its halves of K / V / mean-operand tiles into a 4-stage
+//               ring.
+//   warp 1      MMA issuer (even CTA, one thread): S_g = Q8 K8_g^T and
+//               O_g = P_g R_g (+ M_g mu_g), all with cta_group::2.
+//   warp 2      the per-tile V scales into a 16-slot ring.
 //   warps 4-11  softmax, two threads of one warp per query row (64 scores
-//               each; one shuffle swaps the partial row maxima): row max, alpha,
-//               the ExpCast byte encode (one packed FMA per pair of scores;
-//               the f16-subnormal conversion rounds to the integer code and
-//               clamps it at zero) or exp + E4M3(p * 256); the row mass;
-//               P_j written back over the thread's own S_j columns.
+//               each): row max, alpha, the ExpCast encode (one packed FMA per
+//               pair of scores; the f16-subnormal conversion rounds to the
+//               integer code and clamps it at zero) or exp + E4M3(p * 256),
+//               the row mass; P_g back over its own S_g columns, and with
+//               V-Smooth the row mass as three bf16 pieces beside it.
 //   warps 12-19 correction, two threads per row (64 channels each):
-//               acc = alpha acc + (O_j + M_j mu_j) vscale_j,
-//               den = alpha den + M_j; epilogue acc / den in the output dtype.
+//               acc = alpha acc + O_g vscale_g, den = alpha den + M_g;
+//               epilogue acc / den in the output dtype after each item.
+//
+// V-mean recovery on the tensor core.  The reference adds rowmass * mu_g to
+// PV / 256 before scaling by vscale_g (core.py:334).  Here one extra MMA of
+// kind::f16 (K = 16, bf16 operands) adds M_g mu_g into O_g: A is the row
+// mass split into bf16 pieces M1 + M2 + M3, B the stored mean mu / vscale
+// split into u1 + u2 + u3 (written by the V tile kernel), and the K slots
+// hold the six products Mi uj with i + j <= 4, which carry the FP32 product
+// to about 2^-24.  The correction then does one packed FMA per two channels
+// instead of two, and reads no means.
 //
 // Latency hiding: S and O are double-buffered in TMEM (S0, S1, O0, O1 use all
-// 512 columns).  P_j lives in S_j's columns, so the MMA issues PV_j and then
-// QK_{j+2} into the same buffer (the tensor pipe keeps issue order); QK_{j+2}
-// runs while the softmax works on tile j+1.  PV_j only waits for the
-// correction of tile j-2.  The commit that signals PV_j done (o_full) also
-// tells the producer that K/V stage j % 4 is free.
+// 512 columns).  P_g lives in S_g's columns, so the MMA issues PV_g and then
+// QK_{g+2} into the same buffer (the tensor pipe keeps issue order).  PV_g
+// waits for the correction of tile g - 2 and for K_{g+2}.  The commit that
+// signals PV_g done (o_full, to both CTAs) also frees K/V stage g % 4.
 //
 // Numerical contract (core.py:307-341): S = (q8 . k8) * qs * ks * scale;
 // ExpCast code = rne(clamp(fma(S - m, 8 log2 e, 119.65), 0, 120)) viewed as
@@ -36,7 +56,8 @@
 // inside the accumulator and is rescaled with the running max.  The
 // accumulators are kept in units of 256 (acc256 = 256 acc, den256 = 256
 // den); 256 is a power of two, so no rounding changes.  Every mbarrier wait
-// is bounded (vcb_common.cuh).
+// is bounded (vcb_common.cuh); a CTA that gives up tells its peer, and the
+// pair drains and frees its tensor memory together.
 #include "vcb_internal.h"
 #include <type_traits>
 
@@ -44,35 +65,39 @@ namespace vcb {
 
 namespace {
 
-constexpr int kBM = 128;
-constexpr int kBN = 128;
+constexpr int kBM = 128;                          // query rows per CTA (256 per pair)
+constexpr int kBN = 128;                          // keys per KV tile
 constexpr int kStages = 4;
-constexpr int kMetaSlots = 16;                   // per-tile vscale / mu ring
-constexpr int kThreads = 640;                    // 20 warps: 4 producer/MMA, 8 softmax, 8 correction
-constexpr uint32_t kTile = 128 * 128;            // one E4M3 tile (16 KB)
-constexpr uint32_t kMetaBytes = 1024;            // vscale[128], mu[128]
-constexpr uint32_t kStageBytes = 2 * kTile;      // K tile, V tile
-constexpr uint32_t kOffQ = 0;
-constexpr uint32_t kOffStages = kTile;
-constexpr uint32_t kOffMeta = kOffStages + kStages * kStageBytes;    // vscale[128], mu[128] per slot
-constexpr uint32_t kOffStats = kOffMeta + kMetaSlots * kMetaBytes;   // alpha[4][128], mass[4][2][128]
-constexpr uint32_t kOffBars = kOffStats + 3 * 4 * 128 * 4;
-constexpr int kNumBars = 1 + kStages + 2 * kMetaSlots + 2 * 4 + 2 * 4 + 1;
+constexpr int kMetaSlots = 16;                    // per-tile vscale ring
+constexpr int kThreads = 640;                     // 20 warps: 4 producer/MMA, 8 softmax, 8 correction
+constexpr uint32_t kQBytes = 128 * 128;           // one E4M3 Q tile (16 KB)
+constexpr uint32_t kHalf = 64 * 128;              // this CTA's half of a K or V tile (8 KB)
+constexpr uint32_t kMopHalf = 64 * 32;            // this CTA's half of a mean-operand tile (2 KB)
+constexpr uint32_t kStageBytes = 2 * kHalf + kMopHalf;   // 18 KB, a multiple of 1024
+constexpr uint32_t kOffQ = 0;                     // Q buffers 0, 1
+constexpr uint32_t kOffStages = 2 * kQBytes;
+constexpr uint32_t kMetaBytes = 512;              // vscale[128]
+constexpr uint32_t kOffMeta = kOffStages + kStages * kStageBytes;
+constexpr uint32_t kOffStats = kOffMeta + kMetaSlots * kMetaBytes;  // alpha[4][128], mass[4][128]
+constexpr uint32_t kOffBars = kOffStats + 2 * 4 * 128 * 4;
+constexpr int kNumBars = 2 + 2 + kStages + 2 * kMetaSlots + 4 * 2 + 2 * 4 + 1;
 constexpr uint32_t kOffMisc = kOffBars + kNumBars * 8;
 constexpr uint32_t kSmemBytes = kOffMisc + 16;
 constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS = 0;                    // S0, S1
-constexpr uint32_t kColO = 256;                  // O0, O1
+constexpr uint32_t kColS = 0;                     // S0, S1 (P and the row-mass pieces inside)
+constexpr uint32_t kColO = 256;                   // O0, O1
+constexpr uint32_t kColMass = 16;                 // row-mass operand: S_b columns [16, 24)
+static_assert(kStageBytes % 1024 == 0, "swizzled tiles need 1024-byte aligned stages");
 
-constexpr float kC1 = 11.541560173034668f;       // 8 log2(e) in fp32
-constexpr float kC2 = 119.6500015258789f;        // 119.65 in fp32
-constexpr float kTwoM24 = 5.9604644775390625e-08f;   // 2^-24
+constexpr float kC1 = 11.541560173034668f;        // 8 log2(e) in fp32
+constexpr float kC2 = 119.6500015258789f;         // 119.65 in fp32
+constexpr float kTwoM24 = 5.9604644775390625e-08f;    // 2^-24
 constexpr float kLog2e = 1.4426950408889634f;
-constexpr float kMinNormal = 1.17549435e-38f;    // 2^-126
+constexpr float kMinNormal = 1.17549435e-38f;     // 2^-126
 
 struct Params {
-    CUtensorMap tm_q, tm_k, tm_v;
+    CUtensorMap tm_q, tm_k, tm_v, tm_mop;
     const float* q_scale;
     const float* k_scale;
     const float* v_meta;
@@ -80,6 +105,8 @@ struct Params {
     int32_t* status;
     int64_t sq, sk;
     int dv, q_block, kq, nqb, nkb, T;
+    int pairs;             // pairs of query tiles per head
+    int items;             // heads * pairs
     int out_dtype;
     float scale;
     // diagnostic dump of one CTA's softmax (vcb_attention_fp8_probe)
@@ -90,15 +117,16 @@ struct Params {
 };
 
 struct Bars {
-    uint64_t* q_full;
-    uint64_t* kv_full;     // [kStages]
+    uint64_t* q_full;      // [2]  even CTA: both Q tiles of an item landed
+    uint64_t* q_free;      // [2]  both: the item's QK MMAs are done with Q buffer
+    uint64_t* kv_full;     // [kStages]  even CTA: both halves of K / V (/ mean operand) landed
     uint64_t* meta_full;   // [kMetaSlots]
     uint64_t* meta_empty;  // [kMetaSlots]  the 8 correction warps have read the slot
-    uint64_t* s_full;      // [2]  QK_j done
-    uint64_t* p_full;      // [2]  P_j in TMEM (implies S_j fully read)
-    uint64_t* o_full;      // [2]  PV_j done; also frees K/V stage j % kStages
-    uint64_t* o_free;      // [2]  correction has read O_j
-    uint64_t* st_full;     // [4]  alpha / mass of tile j
+    uint64_t* s_full;      // [2]  both: QK_g done
+    uint64_t* p_full;      // [2]  even CTA: P_g (and the mass pieces) of all 256 rows in TMEM
+    uint64_t* o_full;      // [2]  both: PV_g done; also frees K/V stage g % kStages
+    uint64_t* o_free;      // [2]  even CTA: both corrections have read O_g
+    uint64_t* st_full;     // [4]  alpha / mass of tile g
     uint64_t* st_free;     // [4]
     uint64_t* drain;
 };
@@ -106,7 +134,8 @@ struct Bars {
 __device__ __forceinline__ Bars bars_at(uint8_t* smem) {
     uint64_t* b = reinterpret_cast<uint64_t*>(smem + kOffBars);
     Bars r;
-    r.q_full = b; b += 1;
+    r.q_full = b; b += 2;
+    r.q_free = b; b += 2;
     r.kv_full = b; b += kStages;
     r.meta_full = b; b += kMetaSlots;
     r.meta_empty = b; b += kMetaSlots;
@@ -120,6 +149,66 @@ __device__ __forceinline__ Bars bars_at(uint8_t* smem) {
     return r;
 }
 
+// ------------------------------------------------------------- cluster PTX
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// shared::cluster address of the same shared-memory offset in CTA `rank`
+__device__ __forceinline__ uint32_t peer_addr(const void* p, uint32_t rank) {
+    uint32_t d;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(smem_u32(p)), "r"(rank));
+    return d;
+}
+// arrive on an mbarrier anywhere in the cluster (release at cluster scope)
+__device__ __forceinline__ void mbar_arrive_cluster_if(uint32_t addr, bool pred) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "@p mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];\n\t}"
+        ::"r"(addr), "r"((uint32_t)pred)
+        : "memory");
+}
+__device__ __forceinline__ void store_cluster_u32(uint32_t addr, uint32_t v) {
+    asm volatile("st.relaxed.cluster.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// TMA tile load into this CTA's shared memory whose completion is counted on
+// the even CTA's barrier (`bar` a shared::cluster address); no multicast.
+__device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* map, uint32_t bar, int x, int y,
+                                                 int z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5}], [%2];"
+        ::"r"(smem_u32(dst)), "l"(map), "r"(bar), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"
+                 ::"r"(smem_u32(dst_smem)), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// Arrives on the barrier at this offset in both CTAs once every tcgen05
+// operation this thread issued before is complete.
+__device__ __forceinline__ void commit_both(uint64_t* bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+        ::"r"(smem_u32(bar)), "h"((uint16_t)3)
+        : "memory");
+}
+__device__ __forceinline__ void commit_local_pair(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                 ::"r"(smem_u32(bar)) : "memory");
+}
+
 // Bounded wait used while draining after an abort: ignores the abort flag.
 __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
     const uint32_t a = smem_u32(bar);
@@ -128,6 +217,18 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
         if (globaltimer() - t0 > kWaitLimitNs) return;
     }
 }
+
+// A wait that gives up (mbar_wait) and, when it does, raises the peer CTA's
+// abort flag too, so the pair stops together.
+struct Waiter {
+    volatile int* abort;
+    uint32_t peer_abort;     // shared::cluster address of the other CTA's flag
+    __device__ __forceinline__ bool operator()(uint64_t* bar, uint32_t parity) const {
+        if (mbar_wait(bar, parity, abort)) return true;
+        store_cluster_u32(peer_abort, 1u);
+        return false;
+    }
+};
 
 // 2^x as the single MUFU.EX2 instruction, flushing subnormal results to zero.
 // The softmax's P = 2^g lies in [0, 256]; a result below 2^-126 encodes to
@@ -144,125 +245,211 @@ __device__ __forceinline__ uint32_t cvt_relu_f16x2(float hi, float lo) {
     asm("cvt.rn.relu.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
     return d;
 }
+__device__ __forceinline__ uint32_t cvt_bf16x2(float hi, float lo) {
+    uint32_t d;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+    return d;
+}
 
-__device__ void producer(const Params& p, uint8_t* smem, const Bars& B, volatile int* abort, int qtile,
-                         int head) {
+// The items of cluster `c` are c, c + ncl, ...
+__device__ __forceinline__ int local_items(int items, int c, int ncl) {
+    return c < items ? (items - c + ncl - 1) / ncl : 0;
+}
+
+template <bool HAS_MEAN>
+__device__ void producer(const Params& p, uint8_t* smem, const Bars& B, const Waiter& wait, uint32_t rank, int c,
+                         int ncl) {
     prefetch_tmap(&p.tm_q);
     prefetch_tmap(&p.tm_k);
     prefetch_tmap(&p.tm_v);
-    mbar_arrive_expect_tx(B.q_full, kTile);
-    tma_load_3d(smem + kOffQ, &p.tm_q, B.q_full, 0, qtile * kBM, head);
-    int loaded = 0;
-    for (int j = 0; j < p.T; ++j) {
-        const int s = j % kStages, u = j / kStages;
-        // stage s last held tile j - kStages, free once PV of that tile is done (o_full of its buffer)
-        if (u > 0 && !mbar_wait(&B.o_full[(j - kStages) & 1], ((j - kStages) >> 1) & 1, abort)) break;
-        uint8_t* st = smem + kOffStages + s * kStageBytes;
-        mbar_arrive_expect_tx(&B.kv_full[s], 2 * kTile);
-        tma_load_3d(st, &p.tm_k, &B.kv_full[s], 0, j * kBN, head);
-        tma_load_3d(st + kTile, &p.tm_v, &B.kv_full[s], 0, j * 128, head);
-        loaded = j + 1;
+    if (HAS_MEAN) prefetch_tmap(&p.tm_mop);
+    const uint32_t lead_q = peer_addr(B.q_full, 0);       // q_full[b] at + 8 b
+    const uint32_t lead_kv = peer_addr(B.kv_full, 0);     // kv_full[s] at + 8 s
+    const uint32_t kv_bytes = 2 * (2 * kHalf + (HAS_MEAN ? kMopHalf : 0));
+    uint32_t g = 0, li = 0;
+    int q_loaded = 0;          // items whose Q this CTA has requested
+    uint32_t loaded = 0;       // tiles requested
+    bool ok = true;
+    for (int it = c; ok && it < p.items; it += ncl, ++li) {
+        const int head = it / p.pairs, pair = it - head * p.pairs;
+        const int qb = li & 1;
+        if (li >= 2 && !wait(&B.q_free[qb], ((li - 2) >> 1) & 1)) break;
+        if (rank == 0) mbar_arrive_expect_tx(&B.q_full[qb], 2 * kQBytes);
+        tma_load_3d_pair(smem + kOffQ + qb * kQBytes, &p.tm_q, lead_q + 8 * qb, 0, (2 * pair + (int)rank) * kBM, head);
+        q_loaded = li + 1;
+        for (int j = 0; j < p.T; ++j, ++g) {
+            const int s = g % kStages;
+            // stage s last held tile g - kStages: free once its PV is done
+            if (g >= kStages && !wait(&B.o_full[(g - kStages) & 1], ((g - kStages) >> 1) & 1)) {
+                ok = false;
+                break;
+            }
+            uint8_t* st = smem + kOffStages + s * kStageBytes;
+            if (rank == 0) mbar_arrive_expect_tx(&B.kv_full[s], kv_bytes);
+            const int row = j * kBN + 64 * (int)rank;
+            tma_load_3d_pair(st, &p.tm_k, lead_kv + 8 * s, 0, row, head);
+            tma_load_3d_pair(st + kHalf, &p.tm_v, lead_kv + 8 * s, 0, row, head);
+            if (HAS_MEAN) tma_load_3d_pair(st + 2 * kHalf, &p.tm_mop, lead_kv + 8 * s, 0, row, head);
+            loaded = g + 1;
+        }
     }
-    if (*abort) {   // no TMA write may land after the CTA exits
-        drain_wait(B.q_full, 0);
-        for (int s = 0; s < kStages && s < loaded; ++s)     // last use of stage s: tile s + 4 u
-            drain_wait(&B.kv_full[s], ((loaded - 1 - s) / kStages) & 1);
+    if (*wait.abort) {
+        // No TMA write may land after the pair exits.  The even CTA's barriers
+        // count both CTAs' bytes; the odd CTA gives its copies a bounded
+        // millisecond, far longer than any copy in flight needs.
+        if (rank == 0) {
+            for (int b = 0; b < 2 && b < q_loaded; ++b) drain_wait(&B.q_full[b], ((q_loaded - 1 - b) >> 1) & 1);
+            for (uint32_t s = 0; s < (uint32_t)kStages && s < loaded; ++s)
+                drain_wait(&B.kv_full[s], ((loaded - 1 - s) / kStages) & 1);
+        } else {
+            const uint64_t t0 = globaltimer();
+            while (globaltimer() - t0 < 1000000ull) {
+            }
+        }
     }
 }
 
-// The per-tile V scales and means (1 KB) run on their own deeper ring, so a
-// K/V stage is free as soon as the PV of its tile has been committed.
-__device__ void meta_producer(const Params& p, uint8_t* smem, const Bars& B, volatile int* abort, int head) {
-    const float* meta = p.v_meta + (int64_t)head * p.T * 256;
-    int loaded = 0;
-    for (int j = 0; j < p.T; ++j) {
-        const int s = j % kMetaSlots, u = j / kMetaSlots;
-        if (u > 0 && !mbar_wait(&B.meta_empty[s], (u - 1) & 1, abort)) break;
-        mbar_arrive_expect_tx(&B.meta_full[s], kMetaBytes);
-        bulk_load(smem + kOffMeta + s * kMetaBytes, meta + (int64_t)j * 256, kMetaBytes, &B.meta_full[s]);
-        loaded = j + 1;
+// The per-tile V scales (512 B) run on their own deeper ring, so a K/V stage
+// is free as soon as the PV of its tile has been committed.
+__device__ void meta_producer(const Params& p, uint8_t* smem, const Bars& B, const Waiter& wait, int c, int ncl) {
+    uint32_t g = 0, loaded = 0;
+    bool ok = true;
+    for (int it = c; ok && it < p.items; it += ncl) {
+        const int head = it / p.pairs;
+        const float* meta = p.v_meta + (int64_t)head * p.T * 256;
+        for (int j = 0; j < p.T; ++j, ++g) {
+            const int s = g % kMetaSlots;
+            if (g >= (uint32_t)kMetaSlots && !wait(&B.meta_empty[s], ((g / kMetaSlots) - 1) & 1)) {
+                ok = false;
+                break;
+            }
+            mbar_arrive_expect_tx(&B.meta_full[s], kMetaBytes);
+            bulk_load(smem + kOffMeta + s * kMetaBytes, meta + (int64_t)j * 256, kMetaBytes, &B.meta_full[s]);
+            loaded = g + 1;
+        }
     }
-    if (*abort)
-        for (int s = 0; s < kMetaSlots && s < loaded; ++s)
+    if (*wait.abort)
+        for (uint32_t s = 0; s < (uint32_t)kMetaSlots && s < loaded; ++s)
             drain_wait(&B.meta_full[s], ((loaded - 1 - s) / kMetaSlots) & 1);
 }
 
 // The MMA thread shares its SM sub-partition with four busy softmax /
 // correction warps, and every instruction it issues waits for a scheduler
-// slot (a microbenchmark: 64 cycles per MMA alone, ~270 next to four FMA-bound
-// warps).  So its instruction stream is kept short: shared-memory descriptors
+// slot, so its instruction stream is kept short: shared-memory descriptors
 // differ only in the low word (start address >> 4), which the loop advances
-// by constants; the high word (stride, version, 128B swizzle) is one register.
-__device__ __forceinline__ void mma_ss_lo(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo, uint32_t hi, uint32_t idesc,
-                                          uint32_t accumulate) {
+// by constants; the high word (stride, version, swizzle) is one register.
+__device__ __forceinline__ void mma2_ss(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo, uint32_t hi, uint32_t idesc,
+                                        uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t.reg .b64 da, db;\n\t"
         "mov.b64 da, {%1, %3};\n\t"
         "mov.b64 db, {%2, %3};\n\t"
         "setp.ne.b32 p, %5, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], da, db, %4, p;\n\t}"
+        "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], da, db, %4, p;\n\t}"
         ::"r"(d_tmem), "r"(a_lo), "r"(b_lo), "r"(hi), "r"(idesc), "r"(accumulate)
         : "memory");
 }
-__device__ __forceinline__ void mma_ts_lo(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t hi, uint32_t idesc,
-                                          uint32_t accumulate) {
+__device__ __forceinline__ void mma2_ts(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t hi, uint32_t idesc,
+                                        uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t.reg .b64 db;\n\t"
         "mov.b64 db, {%2, %3};\n\t"
         "setp.ne.b32 p, %5, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], [%1], db, %4, p;\n\t}"
+        "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], [%1], db, %4, p;\n\t}"
         ::"r"(d_tmem), "r"(a_tmem), "r"(b_lo), "r"(hi), "r"(idesc), "r"(accumulate)
         : "memory");
 }
+// D += A B^T with bf16 A in tensor memory and bf16 B in shared memory (K = 16)
+__device__ __forceinline__ void mma2_ts_bf16(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t hi,
+                                             uint32_t idesc) {
+    asm volatile(
+        "{\n\t.reg .b64 db;\n\t"
+        "mov.b64 db, {%2, %3};\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], db, %4, 1;\n\t}"
+        ::"r"(d_tmem), "r"(a_tmem), "r"(b_lo), "r"(hi), "r"(idesc)
+        : "memory");
+}
+
+// Instruction descriptor, kind::f16 with bf16 A and B (format 1 at [7,10)
+// and [10,13)), F32 D, both K-major.
+__host__ __device__ constexpr uint32_t idesc_bf16_f32(int m, int n) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+// Shared-memory descriptor for a K-major operand laid out by a TMA load with
+// 32-byte swizzle: rows of 32 bytes, 8-row atoms 256 bytes apart (SBO),
+// layout type 6 = SWIZZLE_32B at [61,64), version 1 at [46,48).
+__device__ __forceinline__ uint64_t smem_desc_k32(const void* p) {
+    const uint64_t addr = smem_u32(p);
+    return ((addr & 0x3FFFFull) >> 4) | (1ull << 16) | ((256ull >> 4) << 32) | (1ull << 46) | (6ull << 61);
+}
 
 // The tile loop is unrolled by the 4 K/V stages, so stage and TMEM buffer
-// offsets are compile-time constants.
-__device__ void mma_issuer(const Params& p, uint8_t* smem, const Bars& B, volatile int* abort, uint32_t tmem) {
-    const uint32_t idesc = idesc_e4m3_f32(kBM, kBN);
+// offsets are compile-time constants.  g runs over the tiles of all items of
+// this pair; the QK of tile g + 2 is issued right after the PV of tile g.
+template <bool HAS_MEAN>
+__device__ void mma_issuer(const Params& p, uint8_t* smem, const Bars& B, const Waiter& wait, uint32_t tmem, int c,
+                           int ncl) {
+    const uint32_t idesc = idesc_e4m3_f32(2 * kBM, kBN);
+    const uint32_t idesc_mean = idesc_bf16_f32(2 * kBM, kBN);
     const uint64_t q64 = smem_desc_k128(smem + kOffQ);
     const uint32_t hi = (uint32_t)(q64 >> 32);
-    const uint32_t qlo = (uint32_t)q64;
-    // descriptor low word of stage 0's K tile; the others are constant offsets (bytes >> 4)
+    const uint32_t q0lo = (uint32_t)q64;
     const uint32_t k0lo = (uint32_t)smem_desc_k128(smem + kOffStages);
-    constexpr uint32_t kStageLo = kStageBytes >> 4, kTileLo = kTile >> 4;
-    auto qk = [&](uint32_t d, uint32_t klo) {
+    const uint64_t m64 = smem_desc_k32(smem + kOffStages + 2 * kHalf);
+    const uint32_t mhi = (uint32_t)(m64 >> 32), m0lo = (uint32_t)m64;
+    constexpr uint32_t kStageLo = kStageBytes >> 4, kHalfLo = kHalf >> 4, kQLo = kQBytes >> 4;
+    const uint32_t G = (uint32_t)local_items(p.items, c, ncl) * (uint32_t)p.T;
+    // cursor of the next QK: local item and tile
+    uint32_t qli = 0;
+    int qj = 0;
+    auto qk = [&](uint32_t b, uint32_t s2) -> bool {
+        if (qj == 0) {
+            if (!wait(&B.q_full[qli & 1], (qli >> 1) & 1)) return false;
+            tc_fence_after();
+        }
+        const uint32_t qlo = q0lo + (qli & 1) * kQLo, klo = k0lo + s2 * kStageLo;
+        const uint32_t d = tmem + kColS + b * kBN;
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) mma_ss_lo(d, qlo + 2 * kk, klo + 2 * kk, hi, idesc, kk > 0);
-    };
-    bool ok = mbar_wait(B.q_full, 0, abort);
-    for (int j = 0; ok && j < 2 && j < p.T; ++j) {
-        if (!mbar_wait(&B.kv_full[j], 0, abort)) { ok = false; break; }
-        tc_fence_after();
-        qk(tmem + kColS + j * kBN, k0lo + j * kStageLo);
-        mma_commit(&B.s_full[j]);
-    }
-    auto step = [&](auto U_, int j) -> bool {
-        constexpr int U = decltype(U_)::value;       // j % 4
-        constexpr int b = U & 1, s = U, s2 = (U + 2) & 3;
-        if (!mbar_wait(&B.p_full[b], (j >> 1) & 1, abort)) return false;
-        if (j >= 2 && !mbar_wait(&B.o_free[b], ((j - 2) >> 1) & 1, abort)) return false;
-        const bool next = j + 2 < p.T;
-        if (next && !mbar_wait(&B.kv_full[s2], ((j + 2) >> 2) & 1, abort)) return false;
-        tc_fence_after();
-        const uint32_t pa = tmem + kColS + b * kBN;
-        const uint32_t vlo = k0lo + s * kStageLo + kTileLo;
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-            mma_ts_lo(tmem + kColO + b * 128, pa + (kk >> 1) * 64 + (kk & 1) * 8, vlo + 2 * kk, hi, idesc, kk > 0);
-        mma_commit(&B.o_full[b]);      // also frees K/V stage s (the producer waits on it)
-        if (next) {
-            qk(pa, k0lo + s2 * kStageLo);
-            mma_commit(&B.s_full[b]);
+        for (int kk = 0; kk < 4; ++kk) mma2_ss(d, qlo + 2 * kk, klo + 2 * kk, hi, idesc, kk > 0);
+        commit_both(&B.s_full[b]);
+        if (++qj == p.T) {                // the item's last QK: its Q buffer is free once this is done
+            commit_both(&B.q_free[qli & 1]);
+            qj = 0;
+            ++qli;
         }
         return true;
     };
-    for (int j = 0; ok && j < p.T; j += 4) {
-        ok = step(std::integral_constant<int, 0>{}, j);
-        if (ok && j + 1 < p.T) ok = step(std::integral_constant<int, 1>{}, j + 1);
-        if (ok && j + 2 < p.T) ok = step(std::integral_constant<int, 2>{}, j + 2);
-        if (ok && j + 3 < p.T) ok = step(std::integral_constant<int, 3>{}, j + 3);
+    bool ok = true;
+    for (uint32_t g = 0; ok && g < 2 && g < G; ++g) {
+        if (!wait(&B.kv_full[g], 0)) { ok = false; break; }
+        tc_fence_after();
+        ok = qk(g, g);
     }
-    mma_commit(B.drain);
+    auto step = [&](auto U_, uint32_t g) -> bool {
+        constexpr uint32_t U = decltype(U_)::value;      // g % kStages
+        constexpr uint32_t b = U & 1, s = U, s2 = (U + 2) % kStages;
+        if (!wait(&B.p_full[b], (g >> 1) & 1)) return false;
+        if (g >= 2 && !wait(&B.o_free[b], ((g - 2) >> 1) & 1)) return false;
+        const bool next = g + 2 < G;
+        if (next && !wait(&B.kv_full[s2], ((g + 2) / kStages) & 1)) return false;
+        tc_fence_after();
+        const uint32_t pa = tmem + kColS + b * kBN, od = tmem + kColO + b * 128;
+        const uint32_t vlo = k0lo + s * kStageLo + kHalfLo;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) mma2_ts(od, pa + (kk >> 1) * 64 + (kk & 1) * 8, vlo + 2 * kk, hi, idesc, kk > 0);
+        if (HAS_MEAN) mma2_ts_bf16(od, pa + kColMass, m0lo + s * kStageLo, mhi, idesc_mean);
+        commit_both(&B.o_full[b]);       // also frees K/V stage s (the producers wait on it)
+        if (next) return qk(b, s2);
+        return true;
+    };
+    for (uint32_t g = 0; ok && g < G; g += kStages) {
+        ok = step(std::integral_constant<uint32_t, 0>{}, g);
+        if (ok && g + 1 < G) ok = step(std::integral_constant<uint32_t, 1>{}, g + 1);
+        if (ok && g + 2 < G) ok = step(std::integral_constant<uint32_t, 2>{}, g + 2);
+        if (ok && g + 3 < G) ok = step(std::integral_constant<uint32_t, 3>{}, g + 3);
+    }
+    commit_local_pair(B.drain);
     drain_wait(B.drain, 0);
 }
 
@@ -298,228 +485,252 @@ __device__ __forceinline__ void tmem_st16x2_16(uint32_t taddr, const uint32_t (&
           "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
         : "memory");
 }
+// thread t < 16: lane base + t, columns [c, c + 4); thread t + 16: the same
+// lane, columns [c + 4, c + 8): one row's 8 consecutive columns from the pair
+__device__ __forceinline__ void tmem_st16x2_4_split4(uint32_t taddr, uint32_t a, uint32_t b, uint32_t c,
+                                                     uint32_t d) {
+    asm volatile("tcgen05.st.sync.aligned.16x32bx2.x4.b32 [%0], 4, {%1, %2, %3, %4};"
+                 ::"r"(taddr), "r"(a), "r"(b), "r"(c), "r"(d)
+                 : "memory");
+}
 
-template <bool EXPCAST, bool PROBE>
-__device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, volatile int* abort, uint32_t tmem,
-                             int qtile, int head, int quarter, int sub, int lane) {
+template <bool EXPCAST, bool HAS_MEAN, bool PROBE>
+__device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, const Waiter& wait, uint32_t tmem,
+                             uint32_t rank, int c, int ncl, int quarter, int sub, int lane) {
     // warp (quarter, sub) owns rows quarter*32 + sub*16 + [0, 16); lanes t and
     // t + 16 share row t, columns [0, 64) and [64, 128)
     const int hs = lane >> 4;
     const int row = quarter * 32 + sub * 16 + (lane & 15);
-    const int64_t grow = (int64_t)qtile * kBM + row;
-    int qb = (int)(grow / p.q_block);
-    if (qb >= p.nqb) qb = p.nqb - 1;
-    const float qs_scale = p.q_scale[(int64_t)head * p.nqb + qb];
-    const float* ksp = p.k_scale + (int64_t)head * p.nkb;
     float* st_alpha = reinterpret_cast<float*>(smem + kOffStats);
-    float* st_mass = st_alpha + 4 * 128;                       // [4][2][128]
+    float* st_mass = st_alpha + 4 * 128;                        // [4][128]
+    const uint32_t lead_p = peer_addr(B.p_full, 0);            // p_full[b] at + 8 b
     const uint32_t trow = tmem + ((uint32_t)(quarter * 32 + sub * 16) << 16);
     const int kstep = p.kq / kBN;
-    int kidx = 0, kcnt = 0;
-    float m = -INFINITY;
-    for (int j = 0; j < p.T; ++j) {
-        const int b = j & 1;
-        const float ks = __ldg(ksp + kidx);
-        if (++kcnt == kstep) {          // K scale block changes every kq / 128 tiles
-            kcnt = 0;
-            ++kidx;
-        }
-        if (!mbar_wait(&B.s_full[b], (j >> 1) & 1, abort)) break;
-        tc_fence_after();
-        uint32_t r[64];
-        const uint32_t ts = trow + kColS + b * kBN;
-        tmem_ld16x2_at<0>(ts, r);
-        tmem_ld16x2_at<32>(ts + 32, r);
-        tmem_wait_ld();
-        if (j == p.T - 1) {             // only the last tile can be partial
-            const int nvalid = (int)(p.sk - (int64_t)j * kBN) - 64 * hs;
-            if (nvalid < 64) {
-#pragma unroll
-                for (int i = 0; i < 64; ++i)
-                    if (i >= nvalid) r[i] = 0xff800000u;   // -inf: masked key
+    uint32_t g = 0;
+    for (int it = c; it < p.items; it += ncl) {
+        const int head = it / p.pairs, pair = it - head * p.pairs;
+        const int qtile = 2 * pair + (int)rank;
+        const int64_t grow = (int64_t)qtile * kBM + row;
+        int qb = (int)(grow / p.q_block);
+        if (qb >= p.nqb) qb = p.nqb - 1;
+        const float qs_scale = p.q_scale[(int64_t)head * p.nqb + qb];
+        const float* ksp = p.k_scale + (int64_t)head * p.nkb;
+        const bool probe = PROBE && head == p.pr_head && qtile == p.pr_qtile;
+        int kidx = 0, kcnt = 0;
+        float m = -INFINITY;
+        for (int j = 0; j < p.T; ++j, ++g) {
+            const uint32_t b = g & 1;
+            const float ks = __ldg(ksp + kidx);
+            if (++kcnt == kstep) {          // K scale block changes every kq / 128 tiles
+                kcnt = 0;
+                ++kidx;
             }
-        }
-        float mx[4];
+            if (!wait(&B.s_full[b], (g >> 1) & 1)) return;
+            tc_fence_after();
+            uint32_t r[64];
+            const uint32_t ts = trow + kColS + b * kBN;
+            tmem_ld16x2_at<0>(ts, r);
+            tmem_ld16x2_at<32>(ts + 32, r);
+            tmem_wait_ld();
+            if (j == p.T - 1) {             // only the last tile of an item can be partial
+                const int nvalid = (int)(p.sk - (int64_t)j * kBN) - 64 * hs;
+                if (nvalid < 64) {
 #pragma unroll
-        for (int k = 0; k < 4; ++k) mx[k] = fmaxf(__uint_as_float(r[2 * k]), __uint_as_float(r[2 * k + 1]));
+                    for (int i = 0; i < 64; ++i)
+                        if (i >= nvalid) r[i] = 0xff800000u;   // -inf: masked key
+                }
+            }
+            float mx[4];
 #pragma unroll
-        for (int t = 1; t < 8; ++t)
+            for (int k = 0; k < 4; ++k) mx[k] = fmaxf(__uint_as_float(r[2 * k]), __uint_as_float(r[2 * k + 1]));
 #pragma unroll
-            for (int k = 0; k < 4; ++k)
-                mx[k] = fmax3(mx[k], __uint_as_float(r[8 * t + 2 * k]), __uint_as_float(r[8 * t + 2 * k + 1]));
-        const float pmax = fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]);
-        const float omax = __shfl_xor_sync(0xffffffffu, pmax, 16);   // the other half of the row
-        const float rmax = fmaxf(pmax, omax);
-        const float c = __fmul_rn(__fmul_rn(qs_scale, ks), p.scale);
-        const float m_new = fmaxf(m, __fmul_rn(rmax, c));
-        // alpha = e^(m - m_new) as 2^((m - m_new) log2 e) on MUFU.EX2: a few
-        // FP32 ulps from expf, inside the output tolerance, and exactly 1
-        // when the maximum did not move (the correction skips its rescale then)
-        const float alpha = ex2_ftz(__fmul_rn(m - m_new, kLog2e));
-        float A, Bc;
-        // A is kept at or above the smallest normal float: a masked key (-inf)
-        // times A must stay -inf (code 0, no mass), never -inf * 0 = NaN.  When
-        // c underflows that far, every logit s * c is below 2^-100 and the
-        // codes come out as for A = 0, as in the reference.
-        if (EXPCAST) {
-            // in units of 2^-24 throughout: scaling by a power of two is exact,
-            // so this is the unscaled computation times 2^-24, bit for bit
-            A = fmaxf(__fmul_rn(c, kC1 * kTwoM24), kMinNormal);
-            Bc = __fsub_rn(kC2 * kTwoM24, __fmul_rn(m_new, kC1 * kTwoM24));
-            const float umax = fmaf(rmax, A, Bc);
-            if (umax > 120.25f * kTwoM24) Bc = __fsub_rn(Bc, __fsub_rn(umax, kC2 * kTwoM24));
-        } else {
-            A = fmaxf(__fmul_rn(c, kLog2e), kMinNormal);
-            Bc = __fsub_rn(8.0f, __fmul_rn(m_new, kLog2e));
-        }
-        const float2 AA = make_float2(A, A), BB = make_float2(Bc, Bc);
-        float ms[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        uint32_t pk[16];
+            for (int t = 1; t < 8; ++t)
 #pragma unroll
-        for (int w = 0; w < 16; ++w) {
-            const float2 g01 = ffma2(make_float2(__uint_as_float(r[4 * w]), __uint_as_float(r[4 * w + 1])), AA, BB);
-            const float2 g23 =
-                ffma2(make_float2(__uint_as_float(r[4 * w + 2]), __uint_as_float(r[4 * w + 3])), AA, BB);
+                for (int k = 0; k < 4; ++k)
+                    mx[k] = fmax3(mx[k], __uint_as_float(r[8 * t + 2 * k]), __uint_as_float(r[8 * t + 2 * k + 1]));
+            const float pmax = fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]);
+            const float omax = __shfl_xor_sync(0xffffffffu, pmax, 16);   // the other half of the row
+            const float rmax = fmaxf(pmax, omax);
+            const float cs = __fmul_rn(__fmul_rn(qs_scale, ks), p.scale);
+            const float m_new = fmaxf(m, __fmul_rn(rmax, cs));
+            // alpha = e^(m - m_new) as 2^((m - m_new) log2 e) on MUFU.EX2: a few
+            // FP32 ulps from expf, inside the output tolerance, and exactly 1
+            // when the maximum did not move (the correction skips its rescale then)
+            const float alpha = ex2_ftz(__fmul_rn(m - m_new, kLog2e));
+            float A, Bc;
+            // A is kept at or above the smallest normal float: a masked key (-inf)
+            // times A must stay -inf (code 0, no mass), never -inf * 0 = NaN.  When
+            // c underflows that far, every logit s * c is below 2^-100 and the
+            // codes come out as for A = 0, as in the reference.
             if (EXPCAST) {
-                const uint32_t h01 = cvt_relu_f16x2(g01.y, g01.x);   // integer codes as f16 subnormals
-                const uint32_t h23 = cvt_relu_f16x2(g23.y, g23.x);
-                pk[w] = __byte_perm(h01, h23, 0x6420);
-                // code << 7 read as f16 is exactly decode(code) / 256
-                add_f16x2_to_f32(ms[0], ms[1], h01 << 7);
-                add_f16x2_to_f32(ms[2], ms[3], h23 << 7);
+                // in units of 2^-24 throughout: scaling by a power of two is exact,
+                // so this is the unscaled computation times 2^-24, bit for bit
+                A = fmaxf(__fmul_rn(cs, kC1 * kTwoM24), kMinNormal);
+                Bc = __fsub_rn(kC2 * kTwoM24, __fmul_rn(m_new, kC1 * kTwoM24));
+                const float umax = fmaf(rmax, A, Bc);
+                if (umax > 120.25f * kTwoM24) Bc = __fsub_rn(Bc, __fsub_rn(umax, kC2 * kTwoM24));
             } else {
-                const float e0 = ex2_ftz(g01.x), e1 = ex2_ftz(g01.y), e2 = ex2_ftz(g23.x), e3 = ex2_ftz(g23.y);
-                // packed adds: each lane is the same round-to-nearest FP32 add
-                const float2 s01 = fadd2(make_float2(ms[0], ms[1]), make_float2(e0, e1));
-                const float2 s23 = fadd2(make_float2(ms[2], ms[3]), make_float2(e2, e3));
-                ms[0] = s01.x; ms[1] = s01.y; ms[2] = s23.x; ms[3] = s23.y;
-                pk[w] = e4m3x2(e0, e1) | (e4m3x2(e2, e3) << 16);
+                A = fmaxf(__fmul_rn(cs, kLog2e), kMinNormal);
+                Bc = __fsub_rn(8.0f, __fmul_rn(m_new, kLog2e));
             }
-        }
-        // ExpCast: ms holds sum(p) = mass; scale to units of 256.  Otherwise
-        // ms already holds sum(p * 256).
-        float M = __fadd_rn(__fadd_rn(ms[0], ms[1]), __fadd_rn(ms[2], ms[3]));
-        if (EXPCAST) M = __fmul_rn(M, 256.0f);
-        if (PROBE && head == p.pr_head && qtile == p.pr_qtile && j >= p.pr_begin && j < p.pr_begin + p.pr_count) {
-            const int64_t t = j - p.pr_begin;
-            float* lg = p.pr_logits + (t * 128 + row) * 128 + hs * 64;
-            uint32_t* cd = reinterpret_cast<uint32_t*>(p.pr_codes + (t * 128 + row) * 128 + hs * 64);
+            const float2 AA = make_float2(A, A), BB = make_float2(Bc, Bc);
+            float ms[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            uint32_t pk[16];
 #pragma unroll
-            for (int i = 0; i < 64; ++i) lg[i] = __uint_as_float(r[i]);
+            for (int w = 0; w < 16; ++w) {
+                const float2 g01 =
+                    ffma2(make_float2(__uint_as_float(r[4 * w]), __uint_as_float(r[4 * w + 1])), AA, BB);
+                const float2 g23 =
+                    ffma2(make_float2(__uint_as_float(r[4 * w + 2]), __uint_as_float(r[4 * w + 3])), AA, BB);
+                if (EXPCAST) {
+                    const uint32_t h01 = cvt_relu_f16x2(g01.y, g01.x);   // integer codes as f16 subnormals
+                    const uint32_t h23 = cvt_relu_f16x2(g23.y, g23.x);
+                    pk[w] = __byte_perm(h01, h23, 0x6420);
+                    // code << 7 read as f16 is exactly decode(code) / 256
+                    add_f16x2_to_f32(ms[0], ms[1], h01 << 7);
+                    add_f16x2_to_f32(ms[2], ms[3], h23 << 7);
+                } else {
+                    const float e0 = ex2_ftz(g01.x), e1 = ex2_ftz(g01.y), e2 = ex2_ftz(g23.x), e3 = ex2_ftz(g23.y);
+                    // packed adds: each lane is the same round-to-nearest FP32 add
+                    const float2 s01 = fadd2(make_float2(ms[0], ms[1]), make_float2(e0, e1));
+                    const float2 s23 = fadd2(make_float2(ms[2], ms[3]), make_float2(e2, e3));
+                    ms[0] = s01.x; ms[1] = s01.y; ms[2] = s23.x; ms[3] = s23.y;
+                    pk[w] = e4m3x2(e0, e1) | (e4m3x2(e2, e3) << 16);
+                }
+            }
+            // ExpCast: ms holds sum(p) = mass; scale to units of 256.  Otherwise
+            // ms already holds sum(p * 256).  The row's two halves add up to M.
+            float Mh = __fadd_rn(__fadd_rn(ms[0], ms[1]), __fadd_rn(ms[2], ms[3]));
+            if (EXPCAST) Mh = __fmul_rn(Mh, 256.0f);
+            const float M = __fadd_rn(Mh, __shfl_xor_sync(0xffffffffu, Mh, 16));
+            if (probe && j >= p.pr_begin && j < p.pr_begin + p.pr_count) {
+                const int64_t t = j - p.pr_begin;
+                float* lg = p.pr_logits + (t * 128 + row) * 128 + hs * 64;
+                uint32_t* cd = reinterpret_cast<uint32_t*>(p.pr_codes + (t * 128 + row) * 128 + hs * 64);
 #pragma unroll
-            for (int w = 0; w < 16; ++w) cd[w] = pk[w];
+                for (int i = 0; i < 64; ++i) lg[i] = __uint_as_float(r[i]);
+#pragma unroll
+                for (int w = 0; w < 16; ++w) cd[w] = pk[w];
+                if (hs == 0) {
+                    float* rs = p.pr_rowstat + (t * 128 + row) * 4;
+                    rs[0] = m_new; rs[1] = A; rs[2] = Bc; rs[3] = alpha;
+                }
+            }
+            // P_g over this thread's own (already read) S_g columns: 4 codes per
+            // 32-bit column, the A-operand layout of the PV MMA
+            tmem_st16x2_16(ts, pk);
+            if (HAS_MEAN) {
+                // the row mass as bf16 pieces M1 + M2 + M3 (each remainder exact
+                // in FP32), in the K slots [M1, M1, M1, M2, M2, M3, 0 ...] that
+                // meet [u1, u2, u3, u1, u2, u1, 0 ...] of the mean operand
+                const uint32_t p1 = cvt_bf16x2(M, M);
+                const float r1 = __fsub_rn(M, __uint_as_float(p1 << 16));
+                const uint32_t p2 = cvt_bf16x2(r1, r1);
+                const float r2 = __fsub_rn(r1, __uint_as_float(p2 << 16));
+                const uint32_t w1 = __byte_perm(p1, p2, 0x5410);   // (M1, M2)
+                const uint32_t w2 = cvt_bf16x2(r2, r1);              // (M2, M3)
+                tmem_st16x2_4_split4(ts + kColMass, hs ? 0u : p1, hs ? 0u : w1, hs ? 0u : w2, 0u);
+            }
+            const int slot = g & 3;
+            if (g >= 4 && !wait(&B.st_free[slot], ((g >> 2) - 1) & 1)) return;
             if (hs == 0) {
-                float* rs = p.pr_rowstat + (t * 128 + row) * 4;
-                rs[0] = m_new; rs[1] = A; rs[2] = Bc; rs[3] = alpha;
+                st_alpha[slot * 128 + row] = alpha;
+                st_mass[slot * 128 + row] = M;
             }
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            mbar_arrive_cluster_if(lead_p + 8 * b, lane == 0);
+            mbar_arrive_if(&B.st_full[slot], lane == 0);
+            m = m_new;
         }
-        // P_j over this thread's own (already read) S_j columns: 4 codes per
-        // 32-bit column, the A-operand layout of the PV MMA
-        tmem_st16x2_16(ts, pk);
-        const int slot = j & 3;
-        if (j >= 4 && !mbar_wait(&B.st_free[slot], ((j >> 2) - 1) & 1, abort)) break;
-        if (hs == 0) st_alpha[slot * 128 + row] = alpha;
-        st_mass[(slot * 2 + hs) * 128 + row] = M;
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        mbar_arrive_if(&B.p_full[b], lane == 0);
-        mbar_arrive_if(&B.st_full[slot], lane == 0);
-        m = m_new;
     }
 }
 
-template <bool HAS_MEAN>
-__device__ void correction_role(const Params& p, uint8_t* smem, const Bars& B, volatile int* abort,
-                                uint32_t tmem, int qtile, int head, int quarter, int half, int lane) {
+__device__ void correction_role(const Params& p, uint8_t* smem, const Bars& B, const Waiter& wait, uint32_t tmem,
+                                uint32_t rank, int c, int ncl, int quarter, int half, int lane) {
     const int row = quarter * 32 + lane;
     const float* st_alpha = reinterpret_cast<const float*>(smem + kOffStats);
-    const float* st_mass = st_alpha + 4 * 128;          // [4][2][128]
+    const float* st_mass = st_alpha + 4 * 128;
+    const uint32_t lead_o = peer_addr(B.o_free, 0);            // o_free[b] at + 8 b
     const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
     const int c0 = half * 64;
-    float2 acc[32];
+    uint32_t g = 0;
+    for (int it = c; it < p.items; it += ncl) {
+        const int head = it / p.pairs, pair = it - head * p.pairs;
+        const int64_t grow = (int64_t)(2 * pair + (int)rank) * kBM + row;
+        float2 acc[32];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) acc[i] = make_float2(0.0f, 0.0f);
-    float den = 0.0f;
-    bool done = true;
-    for (int j = 0; j < p.T; ++j) {
-        const int b = j & 1, slot = j & 3, s = j % kMetaSlots;
-        if (!mbar_wait(&B.o_full[b], (j >> 1) & 1, abort) ||
-            !mbar_wait(&B.st_full[slot], (j >> 2) & 1, abort) ||
-            !mbar_wait(&B.meta_full[s], (j / kMetaSlots) & 1, abort)) {
-            done = false;
-            break;
-        }
-        tc_fence_after();
-        const float alpha = st_alpha[slot * 128 + row];
-        const float M = __fadd_rn(st_mass[(slot * 2) * 128 + row], st_mass[(slot * 2 + 1) * 128 + row]);
-        __syncwarp();
-        mbar_arrive_if(&B.st_free[slot], lane == 0);
-        const float4* meta = reinterpret_cast<const float4*>(smem + kOffMeta + s * kMetaBytes);
-        const bool rescale = __any_sync(0xffffffffu, alpha != 1.0f);
-        const float2 aa = make_float2(alpha, alpha), MM = make_float2(M, M);
-        const uint32_t to = trow + kColO + b * 128 + c0;
-        if (rescale) {      // warp-uniform; alpha == 1 leaves acc unchanged
+        for (int i = 0; i < 32; ++i) acc[i] = make_float2(0.0f, 0.0f);
+        float den = 0.0f;
+        for (int j = 0; j < p.T; ++j, ++g) {
+            const uint32_t b = g & 1, slot = g & 3, s = g % kMetaSlots;
+            if (!wait(&B.o_full[b], (g >> 1) & 1) || !wait(&B.st_full[slot], (g >> 2) & 1) ||
+                !wait(&B.meta_full[s], (g / kMetaSlots) & 1))
+                return;
+            tc_fence_after();
+            const float alpha = st_alpha[slot * 128 + row];
+            const float M = st_mass[slot * 128 + row];
+            __syncwarp();
+            mbar_arrive_if(&B.st_free[slot], lane == 0);
+            const float4* vsp = reinterpret_cast<const float4*>(smem + kOffMeta + s * kMetaBytes);
+            const bool rescale = __any_sync(0xffffffffu, alpha != 1.0f);
+            const float2 aa = make_float2(alpha, alpha);
+            const uint32_t to = trow + kColO + b * 128 + c0;
+            if (rescale) {      // warp-uniform; alpha == 1 leaves acc unchanged
 #pragma unroll
-            for (int i = 0; i < 32; ++i) acc[i] = fmul2(acc[i], aa);
-        }
-#pragma unroll
-        for (int ch = 0; ch < 2; ++ch) {
-            uint32_t o[32];
-            tmem_ld32_at<0>(to + 32 * ch, o);
-            tmem_wait_ld();
-            if (ch == 1) {
-                tc_fence_before();
-                __syncwarp();
-                mbar_arrive_if(&B.o_free[b], lane == 0);
+                for (int i = 0; i < 32; ++i) acc[i] = fmul2(acc[i], aa);
             }
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
-                const float4 vs = meta[(c0 >> 2) + 8 * ch + q];
-                float4 mu = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (HAS_MEAN) mu = meta[32 + (c0 >> 2) + 8 * ch + q];
+            for (int ch = 0; ch < 2; ++ch) {
+                uint32_t o[32];
+                tmem_ld32_at<0>(to + 32 * ch, o);
+                tmem_wait_ld();
+                if (ch == 1) {
+                    tc_fence_before();
+                    __syncwarp();
+                    mbar_arrive_cluster_if(lead_o + 8 * b, lane == 0);
+                }
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int i = 16 * ch + 2 * q + h;
-                    const int k = 4 * q + 2 * h;
-                    float2 x = make_float2(__uint_as_float(o[k]), __uint_as_float(o[k + 1]));
-                    const float2 v2 = h ? make_float2(vs.z, vs.w) : make_float2(vs.x, vs.y);
-                    if (HAS_MEAN) x = ffma2(MM, h ? make_float2(mu.z, mu.w) : make_float2(mu.x, mu.y), x);
-                    acc[i] = ffma2(x, v2, acc[i]);
+                for (int q = 0; q < 8; ++q) {
+                    const float4 vs = vsp[(c0 >> 2) + 8 * ch + q];
+                    const int i = 16 * ch + 2 * q;
+                    acc[i] = ffma2(make_float2(__uint_as_float(o[4 * q]), __uint_as_float(o[4 * q + 1])),
+                                   make_float2(vs.x, vs.y), acc[i]);
+                    acc[i + 1] = ffma2(make_float2(__uint_as_float(o[4 * q + 2]), __uint_as_float(o[4 * q + 3])),
+                                       make_float2(vs.z, vs.w), acc[i + 1]);
                 }
             }
+            den = __fadd_rn(__fmul_rn(alpha, den), M);
+            __syncwarp();
+            mbar_arrive_if(&B.meta_empty[s], lane == 0);
         }
-        den = __fadd_rn(__fmul_rn(alpha, den), M);
-        __syncwarp();
-        mbar_arrive_if(&B.meta_empty[s], lane == 0);
-    }
-    if (!done) return;
-    const int64_t grow = (int64_t)qtile * kBM + row;
-    if (grow >= p.sq) return;
-    const int64_t base = ((int64_t)head * p.sq + grow) * p.dv;
-    if (p.out_dtype == VCB_BF16 && p.dv == 128) {
-        uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + base + c0);
+        if (grow >= p.sq) continue;
+        const int64_t base = ((int64_t)head * p.sq + grow) * p.dv;
+        if (p.out_dtype == VCB_BF16 && p.dv == 128) {
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + base + c0);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            uint32_t w[4];
+            for (int q = 0; q < 8; ++q) {
+                uint32_t w[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float2 a = acc[4 * q + e];
-                __nv_bfloat162 h2 = __floats2bfloat162_rn(__fdiv_rn(a.x, den), __fdiv_rn(a.y, den));
-                w[e] = *reinterpret_cast<uint32_t*>(&h2);
+                for (int e = 0; e < 4; ++e) {
+                    const float2 a = acc[4 * q + e];
+                    __nv_bfloat162 h2 = __floats2bfloat162_rn(__fdiv_rn(a.x, den), __fdiv_rn(a.y, den));
+                    w[e] = *reinterpret_cast<uint32_t*>(&h2);
+                }
+                dst[q] = make_uint4(w[0], w[1], w[2], w[3]);
             }
-            dst[q] = make_uint4(w[0], w[1], w[2], w[3]);
+            continue;
         }
-        return;
-    }
 #pragma unroll
-    for (int i = 0; i < 64; ++i) {
-        const int col = c0 + i;
-        if (col >= p.dv) break;
-        const float val = __fdiv_rn((i & 1) ? acc[i >> 1].y : acc[i >> 1].x, den);
-        if (p.out_dtype == VCB_BF16) static_cast<__nv_bfloat16*>(p.out)[base + col] = __float2bfloat16_rn(val);
-        else if (p.out_dtype == VCB_F16) static_cast<__half*>(p.out)[base + col] = __float2half_rn(val);
-        else static_cast<float*>(p.out)[base + col] = val;
+        for (int i = 0; i < 64; ++i) {
+            const int col = c0 + i;
+            if (col >= p.dv) break;
+            const float val = __fdiv_rn((i & 1) ? acc[i >> 1].y : acc[i >> 1].x, den);
+            if (p.out_dtype == VCB_BF16) static_cast<__nv_bfloat16*>(p.out)[base + col] = __float2bfloat16_rn(val);
+            else if (p.out_dtype == VCB_F16) static_cast<__half*>(p.out)[base + col] = __float2half_rn(val);
+            else static_cast<float*>(p.out)[base + col] = val;
+        }
     }
 }
 
@@ -527,7 +738,8 @@ template <bool EXPCAST, bool HAS_MEAN, bool PROBE>
 __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant__ Params p) {
     // The swizzled TMA/MMA layouts need a 1024-byte aligned base; the kernel
     // declares no static shared memory, so the dynamic window starts aligned.
-    // Checked anyway: a misaligned window reports an error and does nothing.
+    // Checked anyway: a misaligned window reports an error and does nothing
+    // (both CTAs of a pair see the same offset, so both return here).
     extern __shared__ __align__(1024) uint8_t smem[];
     if (smem_u32(smem) & 1023u) {
         if (threadIdx.x == 0) flag_status(p.status, VCB_FLAG_INTERNAL);
@@ -537,20 +749,22 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffMisc);
     volatile int* abort = reinterpret_cast<volatile int*>(smem + kOffMisc + 4);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int qtile = blockIdx.x, head = blockIdx.y;
+    const uint32_t rank = cluster_rank();
+    const int c = (int)(blockIdx.x >> 1), ncl = (int)(gridDim.x >> 1);
 
     if (threadIdx.x == 0) {
-        mbar_init(B.q_full, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&B.q_full[i], 1);
+            mbar_init(&B.q_free[i], 1);
+            mbar_init(&B.s_full[i], 1);
+            mbar_init(&B.p_full[i], 16);          // 8 softmax warps in each CTA
+            mbar_init(&B.o_full[i], 1);
+            mbar_init(&B.o_free[i], 16);          // 8 correction warps in each CTA
+        }
         for (int s = 0; s < kStages; ++s) mbar_init(&B.kv_full[s], 1);
         for (int s = 0; s < kMetaSlots; ++s) {
             mbar_init(&B.meta_full[s], 1);
-            mbar_init(&B.meta_empty[s], 8);       // 8 correction warps
-        }
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(&B.s_full[b], 1);
-            mbar_init(&B.p_full[b], 8);
-            mbar_init(&B.o_full[b], 1);
-            mbar_init(&B.o_free[b], 8);           // 8 correction warps
+            mbar_init(&B.meta_empty[s], 8);
         }
         for (int s = 0; s < 4; ++s) {
             mbar_init(&B.st_full[s], 8);
@@ -561,33 +775,39 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
         fence_barrier_init();
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, kTmemCols);
-        tmem_relinquish();
+        tmem_alloc_pair(tmem_slot, kTmemCols);
+        tmem_relinquish_pair();
     }
     tc_fence_before();
-    __syncthreads();
+    cluster_sync_all();        // both CTAs' barriers are initialised before any remote arrive or copy
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    const Waiter wait{abort, peer_addr(const_cast<int*>(abort), rank ^ 1u)};
 
-    // Register split of the 640 x 96 launch budget: producer/MMA group 64
-    // (the unrolled MMA loop spills below that), softmax groups 96
-    // (unchanged), correction groups 112; 8192 + 24576 + 28672 = 61440.
+    // Register split of the 640 x 96 launch budget (ptxas allocates each
+    // role's code within its share): producer/MMA group 80 (the unrolled MMA
+    // loop with its item cursor spills below 72), softmax groups 88,
+    // correction groups 112; 10240 + 22528 + 28672 = 61440.
     if (warp < 4) {
-        reg_dealloc<64>();
-        if (warp == 0 && lane == 0) producer(p, smem, B, abort, qtile, head);
-        if (warp == 1 && lane == 0) mma_issuer(p, smem, B, abort, tmem);
-        if (warp == 2 && lane == 0) meta_producer(p, smem, B, abort, head);
+        reg_dealloc<80>();
+        if (warp == 0 && lane == 0) producer<HAS_MEAN>(p, smem, B, wait, rank, c, ncl);
+        if (warp == 1 && lane == 0 && rank == 0) mma_issuer<HAS_MEAN>(p, smem, B, wait, tmem, c, ncl);
+        if (warp == 2 && lane == 0) meta_producer(p, smem, B, wait, c, ncl);
     } else if (warp < 12) {
-        softmax_role<EXPCAST, PROBE>(p, smem, B, abort, tmem, qtile, head, warp & 3, (warp - 4) >> 2, lane);
+        reg_dealloc<88>();
+        softmax_role<EXPCAST, HAS_MEAN, PROBE>(p, smem, B, wait, tmem, rank, c, ncl, warp & 3, (warp - 4) >> 2, lane);
     } else {
         reg_alloc<112>();
-        correction_role<HAS_MEAN>(p, smem, B, abort, tmem, qtile, head, warp & 3, (warp - 12) >> 2, lane);
+        correction_role(p, smem, B, wait, tmem, rank, c, ncl, warp & 3, (warp - 12) >> 2, lane);
     }
     tc_fence_before();
-    __syncthreads();
+    __syncwarp();
+    // No CTA leaves while its peer may still arrive on its barriers, read its
+    // shared memory through an MMA or hold its tensor memory.
+    cluster_sync_all();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, kTmemCols);
+        tmem_dealloc_pair(tmem, kTmemCols);
     }
     if (threadIdx.x == 0 && *abort) flag_status(p.status, VCB_FLAG_TIMEOUT);
 }
@@ -610,28 +830,56 @@ int get_encoder(EncodeTiledFn* fn) {
     return VCB_OK;
 }
 
-// 3-D byte tensor [z][y][128] with 128-byte rows, tiles of 128 x 128, 128B swizzle.
-int make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t planes) {
+// 3-D byte tensor [planes][rows][width] with `width`-byte rows, boxes of
+// width x box_rows, swizzled to the row width (128 B or 32 B).
+int make_map(CUtensorMap* map, const void* base, uint64_t width, uint64_t rows, uint64_t planes, uint32_t box_rows) {
     EncodeTiledFn enc;
     int rc = get_encoder(&enc);
     if (rc) return rc;
-    const cuuint64_t dims[3] = {128, rows, planes};
-    const cuuint64_t strides[2] = {128, 128 * rows};
-    const cuuint32_t box[3] = {128, 128, 1};
+    const cuuint64_t dims[3] = {width, rows, planes};
+    const cuuint64_t strides[2] = {width, width * rows};
+    const cuuint32_t box[3] = {(cuuint32_t)width, box_rows, 1};
     const cuuint32_t estr[3] = {1, 1, 1};
+    const CUtensorMapSwizzle sw = width == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_32B;
     CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(VCB_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
     return VCB_OK;
 }
 
 template <bool E, bool M, bool P>
-int launch(const Params& p, dim3 grid, cudaStream_t st) {
-    VCB_CUDA(cudaFuncSetAttribute(attn_kernel<E, M, P>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)kSmemAlloc));
-    attn_kernel<E, M, P><<<grid, kThreads, kSmemAlloc, st>>>(p);
-    VCB_CUDA(cudaGetLastError());
+int launch(const Params& p, cudaStream_t st) {
+    auto kernel = attn_kernel<E, M, P>;
+    VCB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemAlloc));
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmemAlloc;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    // as many pairs as are resident at once (looked up once per device)
+    int dev = 0;
+    VCB_CUDA(cudaGetDevice(&dev));
+    static int max_clusters[64][8] = {};
+    const int variant = (E ? 4 : 0) | (M ? 2 : 0) | (P ? 1 : 0);
+    if (dev < 0 || dev >= 64) return fail(VCB_ERR_INVALID_ARGUMENT, "device ordinal %d out of range", dev);
+    int& ncl_max = max_clusters[dev][variant];
+    if (ncl_max == 0) {
+        cfg.gridDim = dim3(2 * 148);
+        int n = 0;
+        VCB_CUDA(cudaOccupancyMaxActiveClusters(&n, kernel, &cfg));
+        if (n < 1) return fail(VCB_ERR_CUDA, "the attention kernel's CTA pairs do not fit on this GPU");
+        ncl_max = n;
+    }
+    const int ncl = p.items < ncl_max ? p.items : ncl_max;
+    cfg.gridDim = dim3(2 * ncl);
+    VCB_CUDA(cudaLaunchKernelEx(&cfg, kernel, p));
     return VCB_OK;
 }
 
@@ -695,14 +943,26 @@ __global__ void __launch_bounds__(128, 1)
 }  // namespace
 
 int attn_run(const vcb_attn_args* a, const vcb_attn_probe* probe, cudaStream_t st) {
+    if (a->has_mean && !a->v_mean_op)
+        return fail(VCB_ERR_INVALID_ARGUMENT, "has_mean needs the mean operand (v_mean_op) of vcb_prepare_v");
+    if (a->has_mean && (reinterpret_cast<uintptr_t>(a->v_mean_op) & 15u))
+        return fail(VCB_ERR_INVALID_ARGUMENT, "v_mean_op must be 16-byte aligned");
     Params p;
     memset(&p, 0, sizeof(p));
     const int64_t sq_pad = vcb_padded_rows(a->sq, a->q_block);
     const int64_t sk_pad = vcb_padded_rows(a->sk, a->k_quant_block);
-    const int T = (int)((a->sk + kBN - 1) / kBN);
-    int rc = make_map(&p.tm_q, a->q8, (uint64_t)sq_pad, (uint64_t)a->heads);
-    if (!rc) rc = make_map(&p.tm_k, a->k8, (uint64_t)sk_pad, (uint64_t)a->heads);
-    if (!rc) rc = make_map(&p.tm_v, a->v8, (uint64_t)T * 128, (uint64_t)a->heads);
+    const int64_t T = (a->sk + kBN - 1) / kBN;
+    const int64_t qtiles = (a->sq + kBM - 1) / kBM;
+    const int64_t pairs = (qtiles + 1) / 2;
+    const int64_t items = pairs * a->heads;
+    // the per-pair tile counter is 32-bit: items of one pair x tiles < 2^31
+    // (the grid never has fewer than one pair per 2^31 / T items)
+    if (items >= (1ll << 31) || ((items + 73) / 74) * T >= (1ll << 31))
+        return fail(VCB_ERR_INVALID_ARGUMENT, "problem too large for the attention kernel's tile counters");
+    int rc = make_map(&p.tm_q, a->q8, 128, (uint64_t)sq_pad, (uint64_t)a->heads, kBM);
+    if (!rc) rc = make_map(&p.tm_k, a->k8, 128, (uint64_t)sk_pad, (uint64_t)a->heads, 64);
+    if (!rc) rc = make_map(&p.tm_v, a->v8, 128, (uint64_t)T * 128, (uint64_t)a->heads, 64);
+    if (!rc && a->has_mean) rc = make_map(&p.tm_mop, a->v_mean_op, 32, (uint64_t)T * 128, (uint64_t)a->heads, 64);
     if (rc) return rc;
     p.q_scale = a->q_scale;
     p.k_scale = a->k_scale;
@@ -716,10 +976,11 @@ int attn_run(const vcb_attn_args* a, const vcb_attn_probe* probe, cudaStream_t s
     p.kq = a->k_quant_block;
     p.nqb = (int)((a->sq + a->q_block - 1) / a->q_block);
     p.nkb = (int)((a->sk + a->k_quant_block - 1) / a->k_quant_block);
-    p.T = T;
+    p.T = (int)T;
+    p.pairs = (int)pairs;
+    p.items = (int)items;
     p.out_dtype = a->out_dtype;
     p.scale = a->scale;
-    const dim3 grid((unsigned)((a->sq + kBM - 1) / kBM), (unsigned)a->heads);
     if (probe) {
         p.pr_logits = probe->logits;
         p.pr_codes = probe->codes;
@@ -729,12 +990,11 @@ int attn_run(const vcb_attn_args* a, const vcb_attn_probe* probe, cudaStream_t s
         p.pr_begin = probe->tile_begin;
         p.pr_count = probe->tile_count;
         if (a->expcast)
-            return a->has_mean ? launch<true, true, true>(p, grid, st) : launch<true, false, true>(p, grid, st);
-        return a->has_mean ? launch<false, true, true>(p, grid, st) : launch<false, false, true>(p, grid, st);
+            return a->has_mean ? launch<true, true, true>(p, st) : launch<true, false, true>(p, st);
+        return a->has_mean ? launch<false, true, true>(p, st) : launch<false, false, true>(p, st);
     }
-    if (a->expcast)
-        return a->has_mean ? launch<true, true, false>(p, grid, st) : launch<true, false, false>(p, grid, st);
-    return a->has_mean ? launch<false, true, false>(p, grid, st) : launch<false, false, false>(p, grid, st);
+    if (a->expcast) return a->has_mean ? launch<true, true, false>(p, st) : launch<true, false, false>(p, st);
+    return a->has_mean ? launch<false, true, false>(p, st) : launch<false, false, false>(p, st);
 }
 
 int wait_selftest_run(int complete, const void* src, int32_t* status, int32_t* report, cudaStream_t st) {

@@ -11,7 +11,11 @@
 // interleaved partial sums in tile order, see below), residual, per-channel
 // scale with the mean-dtype finite-storage guard, E4M3 residual written
 // channel-major (the K-major B operand of the PV MMA), and the scaled mean
-// rounded to the mean dtype.
+// rounded to the mean dtype.  With smoothing active the kernel also writes
+// the mean operand of the attention kernel's row-mass x mean MMA: per channel
+// the stored mean as three bf16 pieces (u1 = the value truncated to bf16,
+// u2 and u3 the rounded remainders, so u1 + u2 + u3 carries its 24 bits) laid
+// out as the K = 16 row [u1, u2, u3, u1, u2, u1, 0 ...] (32 bytes).
 #include "vcb_internal.h"
 
 namespace vcb {
@@ -26,7 +30,8 @@ template <typename T>
 __global__ void __launch_bounds__(128) vprep_kernel(const T* __restrict__ v, int64_t S, int dv,
                                                     const int32_t* __restrict__ pi, int active,
                                                     int mean_type, int T_tiles, uint8_t* __restrict__ v8,
-                                                    float* __restrict__ meta, int32_t* status) {
+                                                    float* __restrict__ meta, uint16_t* __restrict__ mop,
+                                                    int32_t* status) {
     extern __shared__ __align__(16) uint8_t tile_raw[];
     T* tile = reinterpret_cast<T*>(tile_raw);     // [kTile][128] in the input type
     const int64_t h = blockIdx.y;
@@ -134,6 +139,16 @@ __global__ void __launch_bounds__(128) vprep_kernel(const T* __restrict__ v, int
         dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
     meta[m * 256 + c] = scale;
     meta[m * 256 + 128 + c] = stored;
+    if (mop) {
+        const __nv_bfloat16 u1 = __float2bfloat16_rz(stored);
+        const float r1 = __fsub_rn(stored, __bfloat162float(u1));          // exact
+        const __nv_bfloat16 u2 = __float2bfloat16_rn(r1);
+        const __nv_bfloat16 u3 = __float2bfloat16_rn(__fsub_rn(r1, __bfloat162float(u2)));   // exact difference
+        const uint32_t b1 = __bfloat16_as_ushort(u1), b2 = __bfloat16_as_ushort(u2), b3 = __bfloat16_as_ushort(u3);
+        uint4* row = reinterpret_cast<uint4*>(mop + (m * 128 + c) * 16);
+        row[0] = make_uint4(b1 | (b2 << 16), b3 | (b1 << 16), b2 | (b1 << 16), 0u);
+        row[1] = make_uint4(0u, 0u, 0u, 0u);
+    }
 }
 
 namespace {
@@ -144,7 +159,7 @@ int launch(const vcb_v_args* p, cudaStream_t st) {
     VCB_CUDA(cudaFuncSetAttribute(vprep_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     vprep_kernel<T><<<dim3(T_tiles, (unsigned)p->heads), 128, smem, st>>>(
         static_cast<const T*>(p->v), p->s, p->dv, p->pi, p->active, p->mean_type, T_tiles, p->v8,
-        p->v_meta, p->status);
+        p->v_meta, p->active ? p->v_mean_op : nullptr, p->status);
     VCB_CUDA(cudaGetLastError());
     return VCB_OK;
 }

@@ -11,7 +11,7 @@ import pathlib
 import threading
 
 LIB_PATH = pathlib.Path(__file__).resolve().parent / "libvcb.so"
-ABI_VERSION = 1
+ABI_VERSION = 2
 NUMERICAL_CONTRACT_VERSION = 2
 
 VCB_OK = 0
@@ -45,12 +45,13 @@ class GroupArgs(ctypes.Structure):
 class VArgs(ctypes.Structure):
     _fields_ = [("v", c_void_p), ("dtype", c_int), ("heads", c_int64), ("s", c_int64), ("dv", c_int),
                 ("pi", c_void_p), ("active", c_int), ("mean_type", c_int), ("kv_block", c_int), ("v8", c_void_p),
-                ("v_meta", c_void_p), ("status", c_void_p)]
+                ("v_meta", c_void_p), ("v_mean_op", c_void_p), ("status", c_void_p)]
 
 
 class AttnArgs(ctypes.Structure):
     _fields_ = [("q8", c_void_p), ("q_scale", c_void_p), ("k8", c_void_p), ("k_scale", c_void_p),
-                ("v8", c_void_p), ("v_meta", c_void_p), ("heads", c_int64), ("sq", c_int64), ("sk", c_int64),
+                ("v8", c_void_p), ("v_meta", c_void_p), ("v_mean_op", c_void_p), ("heads", c_int64),
+                ("sq", c_int64), ("sk", c_int64),
                 ("dv", c_int), ("q_block", c_int), ("k_quant_block", c_int), ("kv_block", c_int),
                 ("expcast", c_int), ("has_mean", c_int), ("scale", c_float), ("out", c_void_p),
                 ("out_dtype", c_int), ("status", c_void_p)]

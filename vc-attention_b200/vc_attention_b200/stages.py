@@ -40,38 +40,42 @@ def quantize_qk(q, k, *, pi=None, q_block=128, k_quant_block=256, k_smooth=True,
 
 
 def prepare_v(v, *, pi=None, active=True, mean_dtype="float16", kv_block=128, status=None):
-    """vcb_prepare_v: returns (v8 [BH, T, 128, 128] u8, v_meta [BH, T, 2, 128] f32)."""
+    """vcb_prepare_v: returns (v8 [BH, T, 128, 128] u8, v_meta [BH, T, 2, 128] f32,
+    mean_op [BH, T, 128, 16] bf16 as uint16, or None when not active)."""
     lib = _extension()
     b, h, s, dv = v.shape
     heads = b * h
     t = -(-s // kv_block)
     v8 = torch.empty((heads, t, 128, kv_block), dtype=torch.uint8, device=v.device)
     meta = torch.empty((heads, t, 2, 128), dtype=torch.float32, device=v.device)
+    mop = torch.empty((heads, t, 128, 16), dtype=torch.int16, device=v.device) if active else None
     vf = _flat(v)
     a = _abi.VArgs(v=vf.data_ptr(), dtype=_DTYPES[v.dtype], heads=heads, s=s, dv=dv, pi=_i(pi), active=int(active),
                    mean_type=_MEAN_TYPES[mean_dtype], kv_block=kv_block, v8=v8.data_ptr(), v_meta=meta.data_ptr(),
-                   status=_i(status))
+                   v_mean_op=_i(mop), status=_i(status))
     with torch.cuda.device(v.device):
         _abi.check(lib, lib.vcb_prepare_v(ctypes.byref(a), _stream(v.device)))
-    return v8, meta
+    return v8, meta, mop
 
 
-def _attn_args(q8, qs, k8, ks, v8, meta, out, *, heads, sq, sk, dv, q_block, k_quant_block, expcast, has_mean,
-               scale, status):
+def _attn_args(q8, qs, k8, ks, v8, meta, mop, out, *, heads, sq, sk, dv, q_block, k_quant_block, expcast,
+               has_mean, scale, status):
     return _abi.AttnArgs(q8=q8.data_ptr(), q_scale=qs.data_ptr(), k8=k8.data_ptr(), k_scale=ks.data_ptr(),
-                         v8=v8.data_ptr(), v_meta=meta.data_ptr(), heads=heads, sq=sq, sk=sk, dv=dv,
+                         v8=v8.data_ptr(), v_meta=meta.data_ptr(), v_mean_op=_i(mop), heads=heads, sq=sq, sk=sk,
+                         dv=dv,
                          q_block=q_block, k_quant_block=k_quant_block, kv_block=128, expcast=int(expcast),
                          has_mean=int(has_mean), scale=float(scale), out=out.data_ptr(),
                          out_dtype=_DTYPES[out.dtype], status=_i(status))
 
 
-def attention_fp8(q8, qs, k8, ks, v8, meta, *, heads, sq, sk, dv, q_block=128, k_quant_block=256, expcast=True,
-                  has_mean=True, scale, out_dtype=torch.bfloat16, out=None, status=None):
-    """vcb_attention_fp8 on prepared operands; returns [heads, sq, dv]."""
+def attention_fp8(q8, qs, k8, ks, v8, meta, *, heads, sq, sk, dv, mean_op=None, q_block=128, k_quant_block=256,
+                  expcast=True, has_mean=True, scale, out_dtype=torch.bfloat16, out=None, status=None):
+    """vcb_attention_fp8 on prepared operands (mean_op: the third output of
+    prepare_v, needed with has_mean); returns [heads, sq, dv]."""
     lib = _extension()
     if out is None:
         out = torch.empty((heads, sq, dv), dtype=out_dtype, device=q8.device)
-    a = _attn_args(q8, qs, k8, ks, v8, meta, out, heads=heads, sq=sq, sk=sk, dv=dv, q_block=q_block,
+    a = _attn_args(q8, qs, k8, ks, v8, meta, mean_op, out, heads=heads, sq=sq, sk=sk, dv=dv, q_block=q_block,
                    k_quant_block=k_quant_block, expcast=expcast, has_mean=has_mean, scale=scale, status=status)
     with torch.cuda.device(q8.device):
         _abi.check(lib, lib.vcb_attention_fp8(ctypes.byref(a), _stream(q8.device)))
@@ -79,7 +83,7 @@ def attention_fp8(q8, qs, k8, ks, v8, meta, *, heads, sq, sk, dv, q_block=128, k
 
 
 def attention_fp8_probe(q8, qs, k8, ks, v8, meta, *, heads, sq, sk, dv, head, q_tile, tile_begin=0,
-                        tile_count=None, q_block=128, k_quant_block=256, expcast=True, has_mean=True, scale,
+                        tile_count=None, mean_op=None, q_block=128, k_quant_block=256, expcast=True, has_mean=True, scale,
                         out_dtype=torch.bfloat16, status=None):
     """vcb_attention_fp8_probe: the full attention plus a dump of one CTA's
     softmax.  Returns (out, logits [n, 128, 128] f32, codes [n, 128, 128] u8,
@@ -92,7 +96,7 @@ def attention_fp8_probe(q8, qs, k8, ks, v8, meta, *, heads, sq, sk, dv, head, q_
     logits = torch.empty((n, 128, 128), dtype=torch.float32, device=dev)
     codes = torch.empty((n, 128, 128), dtype=torch.uint8, device=dev)
     rowstat = torch.empty((n, 128, 4), dtype=torch.float32, device=dev)
-    a = _attn_args(q8, qs, k8, ks, v8, meta, out, heads=heads, sq=sq, sk=sk, dv=dv, q_block=q_block,
+    a = _attn_args(q8, qs, k8, ks, v8, meta, mean_op, out, heads=heads, sq=sq, sk=sk, dv=dv, q_block=q_block,
                    k_quant_block=k_quant_block, expcast=expcast, has_mean=has_mean, scale=scale, status=status)
     pr = _abi.AttnProbe(head=head, q_tile=q_tile, tile_begin=tile_begin, tile_count=n, logits=logits.data_ptr(),
                         codes=codes.data_ptr(), rowstat=rowstat.data_ptr())

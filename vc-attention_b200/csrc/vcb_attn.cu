@@ -78,9 +78,10 @@ constexpr uint32_t kOffQ = 0;                     // Q buffers 0, 1
 constexpr uint32_t kOffStages = 2 * kQBytes;
 constexpr uint32_t kMetaBytes = 512;              // vscale[128]
 constexpr uint32_t kOffMeta = kOffStages + kStages * kStageBytes;
-constexpr uint32_t kOffStats = kOffMeta + kMetaSlots * kMetaBytes;  // alpha[4][128], mass[4][128]
-constexpr uint32_t kOffBars = kOffStats + 2 * 4 * 128 * 4;
-constexpr int kNumBars = 2 + 2 + kStages + 2 * kMetaSlots + 4 * 2 + 2 * 4 + 1;
+constexpr int kStatSlots = 8;                     // per-tile alpha / row-mass ring
+constexpr uint32_t kOffStats = kOffMeta + kMetaSlots * kMetaBytes;  // alpha[8][128], mass[8][128]
+constexpr uint32_t kOffBars = kOffStats + 2 * kStatSlots * 128 * 4;
+constexpr int kNumBars = 2 + 2 + kStages + 2 * kMetaSlots + 4 * 2 + 2 * kStatSlots + 2;
 constexpr uint32_t kOffMisc = kOffBars + kNumBars * 8;
 constexpr uint32_t kSmemBytes = kOffMisc + 16;
 constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;
@@ -126,9 +127,9 @@ struct Bars {
     uint64_t* p_full;      // [2]  even CTA: P_g (and the mass pieces) of all 256 rows in TMEM
     uint64_t* o_full;      // [2]  both: PV_g done; also frees K/V stage g % kStages
     uint64_t* o_free;      // [2]  even CTA: both corrections have read O_g
-    uint64_t* st_full;     // [4]  alpha / mass of tile g
-    uint64_t* st_free;     // [4]
-    uint64_t* drain;
+    uint64_t* st_full;     // [kStatSlots]  alpha / mass of tile g
+    uint64_t* st_free;     // [kStatSlots]
+    uint64_t* drain;       // [2]  one per MMA thread
 };
 
 __device__ __forceinline__ Bars bars_at(uint8_t* smem) {
@@ -143,8 +144,8 @@ __device__ __forceinline__ Bars bars_at(uint8_t* smem) {
     r.p_full = b; b += 2;
     r.o_full = b; b += 2;
     r.o_free = b; b += 2;
-    r.st_full = b; b += 4;
-    r.st_free = b; b += 4;
+    r.st_full = b; b += kStatSlots;
+    r.st_free = b; b += kStatSlots;
     r.drain = b;
     return r;
 }
@@ -161,12 +162,16 @@ __device__ __forceinline__ uint32_t peer_addr(const void* p, uint32_t rank) {
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(smem_u32(p)), "r"(rank));
     return d;
 }
-// arrive on an mbarrier anywhere in the cluster (release at cluster scope)
+// Arrive on an mbarrier anywhere in the cluster, with the default
+// (CTA-scope) release.  The data these arrivals publish is tensor memory,
+// ordered for the MMA by tcgen05.wait::st / tcgen05.fence::before_thread_sync
+// before the arrive and tcgen05.fence::after_thread_sync after the wait; a
+// cluster-scope release here cost ~1000 cycles per tile.
 __device__ __forceinline__ void mbar_arrive_cluster_if(uint32_t addr, bool pred) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.u32 p, %1, 0;\n\t"
-        "@p mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];\n\t}"
+        "@p mbarrier.arrive.shared::cluster.b64 _, [%0];\n\t}"
         ::"r"(addr), "r"((uint32_t)pred)
         : "memory");
 }
@@ -384,12 +389,20 @@ __device__ __forceinline__ uint64_t smem_desc_k32(const void* p) {
     return ((addr & 0x3FFFFull) >> 4) | (1ull << 16) | ((256ull >> 4) << 32) | (1ull << 46) | (6ull << 61);
 }
 
-// The tile loop is unrolled by the 4 K/V stages, so stage and TMEM buffer
-// offsets are compile-time constants.  g runs over the tiles of all items of
-// this pair; the QK of tile g + 2 is issued right after the PV of tile g.
-template <bool HAS_MEAN>
+// Two MMA threads of the even CTA, on different SM sub-partitions, split the
+// issue work: thread X (warp 1 for X = 0, warp 3 for X = 1) owns TMEM buffers
+// S_X / O_X and issues PV_g then QK_{g+2} for the tiles g of its parity, g
+// running over the tiles of all items of this pair.  No accumulator is shared
+// between the threads, so the tensor pipe may interleave their MMAs freely;
+// each thread's own issue order keeps QK_{g+2} after the PV_g that reads P_g
+// from the same buffer.  Every MMA instruction waits for issue slots next to
+// the busy softmax and correction warps, so two issuers halve the per-tile
+// issue latency on the critical path.  The loop is unrolled by the thread's
+// two K/V stages (X and X + 2), so stage and buffer offsets are constants.
+template <bool HAS_MEAN, uint32_t X>
 __device__ void mma_issuer(const Params& p, uint8_t* smem, const Bars& B, const Waiter& wait, uint32_t tmem, int c,
                            int ncl) {
+    static_assert(kStages == 4, "two issuers with two stages each");
     const uint32_t idesc = idesc_e4m3_f32(2 * kBM, kBN);
     const uint32_t idesc_mean = idesc_bf16_f32(2 * kBM, kBN);
     const uint64_t q64 = smem_desc_k128(smem + kOffQ);
@@ -399,58 +412,64 @@ __device__ void mma_issuer(const Params& p, uint8_t* smem, const Bars& B, const 
     const uint64_t m64 = smem_desc_k32(smem + kOffStages + 2 * kHalf);
     const uint32_t mhi = (uint32_t)(m64 >> 32), m0lo = (uint32_t)m64;
     constexpr uint32_t kStageLo = kStageBytes >> 4, kHalfLo = kHalf >> 4, kQLo = kQBytes >> 4;
-    const uint32_t G = (uint32_t)local_items(p.items, c, ncl) * (uint32_t)p.T;
-    // cursor of the next QK: local item and tile
-    uint32_t qli = 0;
-    int qj = 0;
-    auto qk = [&](uint32_t b, uint32_t s2) -> bool {
-        if (qj == 0) {
+    const uint32_t T = (uint32_t)p.T;
+    const uint32_t G = (uint32_t)local_items(p.items, c, ncl) * T;
+    const uint32_t d = tmem + kColS + X * kBN, od = tmem + kColO + X * 128;
+    // cursor of this thread's next QK: local item and tile; every item the
+    // cursor leaves gets this thread's q_free arrival (count 2: both threads)
+    uint32_t qli = 0, qj = X, q_waited = 0xffffffffu;
+    while (qj >= T) {                   // an item of one tile holds no QK of thread 1
+        qj -= T;
+        commit_both(&B.q_free[qli & 1]);
+        ++qli;
+    }
+    auto qk = [&](uint32_t s2) -> bool {
+        if (qli != q_waited) {
             if (!wait(&B.q_full[qli & 1], (qli >> 1) & 1)) return false;
             tc_fence_after();
+            q_waited = qli;
         }
         const uint32_t qlo = q0lo + (qli & 1) * kQLo, klo = k0lo + s2 * kStageLo;
-        const uint32_t d = tmem + kColS + b * kBN;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) mma2_ss(d, qlo + 2 * kk, klo + 2 * kk, hi, idesc, kk > 0);
-        commit_both(&B.s_full[b]);
-        if (++qj == p.T) {                // the item's last QK: its Q buffer is free once this is done
+        commit_both(&B.s_full[X]);
+        qj += 2;
+        while (qj >= T) {               // this thread's QKs of item qli are all issued
+            qj -= T;
             commit_both(&B.q_free[qli & 1]);
-            qj = 0;
             ++qli;
         }
         return true;
     };
     bool ok = true;
-    for (uint32_t g = 0; ok && g < 2 && g < G; ++g) {
-        if (!wait(&B.kv_full[g], 0)) { ok = false; break; }
-        tc_fence_after();
-        ok = qk(g, g);
+    if (X < G) {
+        ok = wait(&B.kv_full[X], 0);
+        if (ok) {
+            tc_fence_after();
+            ok = qk(X);
+        }
     }
-    auto step = [&](auto U_, uint32_t g) -> bool {
-        constexpr uint32_t U = decltype(U_)::value;      // g % kStages
-        constexpr uint32_t b = U & 1, s = U, s2 = (U + 2) % kStages;
-        if (!wait(&B.p_full[b], (g >> 1) & 1)) return false;
-        if (g >= 2 && !wait(&B.o_free[b], ((g - 2) >> 1) & 1)) return false;
+    auto step = [&](auto S_, uint32_t g) -> bool {
+        constexpr uint32_t s = decltype(S_)::value, s2 = (s + 2) % kStages;   // g % kStages
+        if (!wait(&B.p_full[X], (g >> 1) & 1)) return false;
+        if (g >= 2 && !wait(&B.o_free[X], ((g - 2) >> 1) & 1)) return false;
         const bool next = g + 2 < G;
         if (next && !wait(&B.kv_full[s2], ((g + 2) / kStages) & 1)) return false;
         tc_fence_after();
-        const uint32_t pa = tmem + kColS + b * kBN, od = tmem + kColO + b * 128;
         const uint32_t vlo = k0lo + s * kStageLo + kHalfLo;
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) mma2_ts(od, pa + (kk >> 1) * 64 + (kk & 1) * 8, vlo + 2 * kk, hi, idesc, kk > 0);
-        if (HAS_MEAN) mma2_ts_bf16(od, pa + kColMass, m0lo + s * kStageLo, mhi, idesc_mean);
-        commit_both(&B.o_full[b]);       // also frees K/V stage s (the producers wait on it)
-        if (next) return qk(b, s2);
+        for (int kk = 0; kk < 4; ++kk) mma2_ts(od, d + (kk >> 1) * 64 + (kk & 1) * 8, vlo + 2 * kk, hi, idesc, kk > 0);
+        if (HAS_MEAN) mma2_ts_bf16(od, d + kColMass, m0lo + s * kStageLo, mhi, idesc_mean);
+        commit_both(&B.o_full[X]);       // also frees K/V stage s (the producers wait on it)
+        if (next) return qk(s2);
         return true;
     };
-    for (uint32_t g = 0; ok && g < G; g += kStages) {
-        ok = step(std::integral_constant<uint32_t, 0>{}, g);
-        if (ok && g + 1 < G) ok = step(std::integral_constant<uint32_t, 1>{}, g + 1);
-        if (ok && g + 2 < G) ok = step(std::integral_constant<uint32_t, 2>{}, g + 2);
-        if (ok && g + 3 < G) ok = step(std::integral_constant<uint32_t, 3>{}, g + 3);
+    for (uint32_t g = X; ok && g < G; g += 4) {
+        ok = step(std::integral_constant<uint32_t, X>{}, g);
+        if (ok && g + 2 < G) ok = step(std::integral_constant<uint32_t, X + 2>{}, g + 2);
     }
-    commit_local_pair(B.drain);
-    drain_wait(B.drain, 0);
+    commit_local_pair(&B.drain[X]);
+    drain_wait(&B.drain[X], 0);
 }
 
 // Two threads of one warp per query row: warp w (quarter w % 4, sub (w-4)/4)
@@ -485,6 +504,16 @@ __device__ __forceinline__ void tmem_st16x2_16(uint32_t taddr, const uint32_t (&
           "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
         : "memory");
 }
+// 32 lanes x 16 consecutive 32-bit columns; thread i of the warp gets lane i
+__device__ __forceinline__ void tmem_ld32x16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+
 // thread t < 16: lane base + t, columns [c, c + 4); thread t + 16: the same
 // lane, columns [c + 4, c + 8): one row's 8 consecutive columns from the pair
 __device__ __forceinline__ void tmem_st16x2_4_split4(uint32_t taddr, uint32_t a, uint32_t b, uint32_t c,
@@ -502,7 +531,7 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, cons
     const int hs = lane >> 4;
     const int row = quarter * 32 + sub * 16 + (lane & 15);
     float* st_alpha = reinterpret_cast<float*>(smem + kOffStats);
-    float* st_mass = st_alpha + 4 * 128;                        // [4][128]
+    float* st_mass = st_alpha + kStatSlots * 128;               // [kStatSlots][128]
     const uint32_t lead_p = peer_addr(B.p_full, 0);            // p_full[b] at + 8 b
     const uint32_t trow = tmem + ((uint32_t)(quarter * 32 + sub * 16) << 16);
     const int kstep = p.kq / kBN;
@@ -525,10 +554,10 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, cons
                 kcnt = 0;
                 ++kidx;
             }
+            const uint32_t ts = trow + kColS + b * kBN;
             if (!wait(&B.s_full[b], (g >> 1) & 1)) return;
             tc_fence_after();
             uint32_t r[64];
-            const uint32_t ts = trow + kColS + b * kBN;
             tmem_ld16x2_at<0>(ts, r);
             tmem_ld16x2_at<32>(ts + 32, r);
             tmem_wait_ld();
@@ -631,8 +660,8 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, cons
                 const uint32_t w2 = cvt_bf16x2(r2, r1);              // (M2, M3)
                 tmem_st16x2_4_split4(ts + kColMass, hs ? 0u : p1, hs ? 0u : w1, hs ? 0u : w2, 0u);
             }
-            const int slot = g & 3;
-            if (g >= 4 && !wait(&B.st_free[slot], ((g >> 2) - 1) & 1)) return;
+            const int slot = g % kStatSlots;
+            if (g >= (uint32_t)kStatSlots && !wait(&B.st_free[slot], ((g / kStatSlots) - 1) & 1)) return;
             if (hs == 0) {
                 st_alpha[slot * 128 + row] = alpha;
                 st_mass[slot * 128 + row] = M;
@@ -651,7 +680,7 @@ __device__ void correction_role(const Params& p, uint8_t* smem, const Bars& B, c
                                 uint32_t rank, int c, int ncl, int quarter, int half, int lane) {
     const int row = quarter * 32 + lane;
     const float* st_alpha = reinterpret_cast<const float*>(smem + kOffStats);
-    const float* st_mass = st_alpha + 4 * 128;
+    const float* st_mass = st_alpha + kStatSlots * 128;
     const uint32_t lead_o = peer_addr(B.o_free, 0);            // o_free[b] at + 8 b
     const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
     const int c0 = half * 64;
@@ -664,8 +693,8 @@ __device__ void correction_role(const Params& p, uint8_t* smem, const Bars& B, c
         for (int i = 0; i < 32; ++i) acc[i] = make_float2(0.0f, 0.0f);
         float den = 0.0f;
         for (int j = 0; j < p.T; ++j, ++g) {
-            const uint32_t b = g & 1, slot = g & 3, s = g % kMetaSlots;
-            if (!wait(&B.o_full[b], (g >> 1) & 1) || !wait(&B.st_full[slot], (g >> 2) & 1) ||
+            const uint32_t b = g & 1, slot = g % kStatSlots, s = g % kMetaSlots;
+            if (!wait(&B.o_full[b], (g >> 1) & 1) || !wait(&B.st_full[slot], (g / kStatSlots) & 1) ||
                 !wait(&B.meta_full[s], (g / kMetaSlots) & 1))
                 return;
             tc_fence_after();
@@ -755,7 +784,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
     if (threadIdx.x == 0) {
         for (int i = 0; i < 2; ++i) {
             mbar_init(&B.q_full[i], 1);
-            mbar_init(&B.q_free[i], 1);
+            mbar_init(&B.q_free[i], 2);           // both MMA threads
+            mbar_init(&B.drain[i], 1);
             mbar_init(&B.s_full[i], 1);
             mbar_init(&B.p_full[i], 16);          // 8 softmax warps in each CTA
             mbar_init(&B.o_full[i], 1);
@@ -766,11 +796,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
             mbar_init(&B.meta_full[s], 1);
             mbar_init(&B.meta_empty[s], 8);
         }
-        for (int s = 0; s < 4; ++s) {
+        for (int s = 0; s < kStatSlots; ++s) {
             mbar_init(&B.st_full[s], 8);
             mbar_init(&B.st_free[s], 8);
         }
-        mbar_init(B.drain, 1);
         *abort = 0;
         fence_barrier_init();
     }
@@ -791,7 +820,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
     if (warp < 4) {
         reg_dealloc<80>();
         if (warp == 0 && lane == 0) producer<HAS_MEAN>(p, smem, B, wait, rank, c, ncl);
-        if (warp == 1 && lane == 0 && rank == 0) mma_issuer<HAS_MEAN>(p, smem, B, wait, tmem, c, ncl);
+        if (warp == 1 && lane == 0 && rank == 0) mma_issuer<HAS_MEAN, 0>(p, smem, B, wait, tmem, c, ncl);
+        if (warp == 3 && lane == 0 && rank == 0) mma_issuer<HAS_MEAN, 1>(p, smem, B, wait, tmem, c, ncl);
         if (warp == 2 && lane == 0) meta_producer(p, smem, B, wait, c, ncl);
     } else if (warp < 12) {
         reg_dealloc<88>();

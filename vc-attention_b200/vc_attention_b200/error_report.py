@@ -101,8 +101,74 @@ def report(*, config="c2", heads=2, seq=4096, seed=0, modes=tuple(MODES), rows=6
     return out
 
 
+def load_capture(path):
+    """Q/K/V and metadata of a capture written by ``lightx2v.capture`` (or by
+    the reference adapter, lightx2v.py:92-125), with the file's identity as
+    the reference's replay records it (replay.py:80-89)."""
+    import hashlib
+    from pathlib import Path
+
+    path = Path(path)
+    record = torch.load(path, map_location="cpu", weights_only=True)
+    q, k, v = (record[name] for name in ("q", "k", "v"))
+    source = {"kind": "captured_qkv", "file": str(path.resolve()),
+              "sha256": hashlib.sha256(path.read_bytes()).hexdigest(), "metadata": record["metadata"]}
+    return q, k, v, source
+
+
+def query_slice(q, q_start, q_limit):
+    """Rows [q_start, q_start + q_limit) of Q (all rows from q_start when
+    q_limit is 0); q_start must be a 128-row block boundary inside Q, so the
+    slice's Q blocks quantise exactly as in the full call (replay.py:92-96).
+    K and V are never cropped."""
+    if q_start % 128 or not 0 <= q_start < q.shape[-2]:
+        raise ValueError("q-start must be a valid 128-token block boundary")
+    end = q.shape[-2] if q_limit == 0 else min(q.shape[-2], q_start + q_limit)
+    return q[..., q_start:end, :]
+
+
+def replay(path, *, modes=tuple(MODES), rows=64, q_start=0, q_limit=0, device="cuda", reference_device="cpu"):
+    """The error report on a captured post-RoPE Q/K/V (replay.py:80-96): the
+    capture's softmax scale and step, a 128-aligned query slice against the
+    full K/V, each mode's native output against the FP64 softmax of the same
+    rows (and against the upstream reference backend when importable)."""
+    from . import Config, attention
+
+    q, k, v, source = load_capture(path)
+    meta = source["metadata"]
+    scale, step, total = float(meta["scale"]), int(meta.get("step", 0)), int(meta.get("total_steps", 1))
+    q = query_slice(q, q_start, q_limit)
+    q, k, v = (x.to(device) for x in (q, k, v))
+    ids = query_rows(q.shape[2], rows)
+    golden = fp32_golden(q, k, v, ids, scale).cpu()
+    upstream = _upstream_reference()
+    pick = torch.tensor(ids)
+    out = {"source": source, "q_start": q_start, "q_rows": q.shape[2], "kv_tokens": k.shape[2],
+           "rows": len(ids), "step": step, "total_steps": total,
+           "reference": "vc_attention" if upstream else "not importable", "modes": {}}
+    for mode in modes:
+        smooth, cast = MODES[mode]
+        native, stats = attention(q, k, v, Config(v_smooth=smooth, expcast=cast), step=step, total_steps=total,
+                                  scale=scale)
+        native = native.float().cpu().index_select(2, pick)
+        entry = {"native_vs_fp32": metrics(native, golden), "smoothing_active": stats["smoothing_active"]}
+        if upstream:
+            ref_config, ref_attention = upstream
+            rq, rk, rv = (x.to(reference_device) for x in (q, k, v))
+            ref, _ = ref_attention(rq, rk, rv, ref_config(v_smooth=smooth, expcast=cast, backend="reference"),
+                                   step=step, total_steps=total, scale=scale)
+            ref = ref.float().cpu().index_select(2, pick)
+            entry["reference_vs_fp32"] = metrics(ref, golden)
+            entry["native_vs_reference"] = metrics(native, ref)
+        out["modes"][mode] = entry
+    return out
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
+    ap.add_argument("--capture", help="replay a captured Q/K/V file instead of the synthetic inputs")
+    ap.add_argument("--q-start", type=int, default=0, help="with --capture: first query row (multiple of 128)")
+    ap.add_argument("--q-limit", type=int, default=0, help="with --capture: query rows (0 = to the end)")
     ap.add_argument("--config", default="c2", choices=("c1", "c2", "c3", "c4", "c5"))
     ap.add_argument("--heads", type=int, default=2)
     ap.add_argument("--seq", type=int, default=4096)
@@ -116,6 +182,13 @@ def main(argv=None):
     a = ap.parse_args(argv)
     if a.rows < 1 or a.heads < 1 or a.seq < 1 or not 0 <= a.step < a.total_steps:
         ap.error("rows, heads and seq must be positive and 0 <= step < total-steps")
+    if a.capture:
+        if a.q_start % 128 or a.q_start < 0 or a.q_limit < 0:
+            ap.error("q-start must be a non-negative multiple of 128 and q-limit non-negative")
+        res = replay(a.capture, modes=tuple(a.mode or MODES), rows=a.rows, q_start=a.q_start, q_limit=a.q_limit,
+                     device=a.device, reference_device=a.reference_device)
+        print(json.dumps(res, indent=2))
+        return 0
     res = report(config=a.config, heads=a.heads, seq=a.seq, seed=a.seed, modes=tuple(a.mode or MODES),
                  rows=a.rows, step=a.step, total_steps=a.total_steps, device=a.device,
                  reference_device=a.reference_device)

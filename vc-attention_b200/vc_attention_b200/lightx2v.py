@@ -2,10 +2,10 @@
 
 The reference ships an opt-in adapter that a LightX2V video DiT calls for every
 self-attention layer (src/vc_attention/lightx2v.py:38-125).  It checks the call
-layout, keeps one ``LayoutCache`` per generation, guards the layer/step order
-and counts what the backend did.  Its capture and MindIE arms target Ascend
-NPUs and are not part of this package.  This module keeps the same contract on
-a B200:
+layout, keeps one ``LayoutCache`` per generation, guards the layer/step order,
+counts what the backend did and can capture the post-RoPE Q/K/V of chosen
+layers and steps for offline replay.  Its MindIE arms target Ascend NPUs and
+are not part of this package.  This module keeps the same contract on a B200:
 
 * ``validate_layout`` accepts one dense, non-causal, unmasked self-attention
   sequence in SND or 1SND layout and returns BNSD views
@@ -15,6 +15,10 @@ a B200:
   marker changes or layer ``l`` comes back at step 0, refuses repeated or
   reversed (layer, step) pairs, runs ``attention`` and returns ``[S, H*D]`` in
   the input dtype (lightx2v.py:48-96).
+* With ``CaptureOptions`` it also saves the first heads of the post-RoPE
+  Q/K/V of the chosen (rank, step, layer) calls, within a byte budget, as
+  ``captures/rank{r}_step{s}_layer{l}.pt`` with the reference's metadata
+  (lightx2v.py:92-125); ``error_report --capture`` replays such a file.
 * ``configure`` checks and patches a LightX2V JSON config
   (lightx2v.py:128-144).
 * ``main`` writes the patched config, registers the adapter with LightX2V's
@@ -31,7 +35,7 @@ import json
 import os
 import runpy
 import sys
-from dataclasses import asdict
+from dataclasses import asdict, dataclass, field
 from pathlib import Path
 
 import torch
@@ -72,7 +76,58 @@ def validate_layout(q, k, v, cu_seqlens_q, cu_seqlens_kv, max_seqlen_q, max_seql
 
 def _new_audit(mode):
     return {"mode": mode, "backend": "b200_fp8", "status": "running", "calls": 0, "smoothing_calls": 0,
-            "regroup_calls": 0, "expcast_calls": 0}
+            "regroup_calls": 0, "expcast_calls": 0, "captures": {}, "capture_bytes": 0}
+
+
+@dataclass
+class CaptureOptions:
+    """Which attention calls to save and how much (the reference's
+    --capture-* options and their defaults, lightx2v.py:153-158, :167)."""
+    output_dir: str
+    steps: tuple = (0, 4)
+    layers: tuple = (0, 12)
+    rank: int = 0
+    heads: int = 1
+    max_captures: int = 4
+    max_capture_mib: int = 512
+    model: str = "unspecified"
+    extra: dict = field(default_factory=dict)
+
+    def __post_init__(self):
+        if min(self.heads, self.max_captures, self.max_capture_mib) < 1:
+            raise ValueError("capture heads, max-captures and max-capture-mib must be positive")
+
+
+def capture(options, audit, q, k, v, *, step, steps, layer, scale, rank=None):
+    """Save the first ``options.heads`` heads of BNSD post-RoPE Q/K/V for one
+    (rank, step, layer) call, as the reference's ``_capture`` does
+    (lightx2v.py:92-125): one file per key, at most ``max_captures`` files,
+    and a ValueError rather than a silent skip when the byte budget would be
+    exceeded.  Returns the path written, or None when the call is not
+    selected."""
+    rank = int(os.environ.get("RANK", "0")) if rank is None else rank
+    if rank != options.rank or step not in options.steps or layer not in options.layers:
+        return None
+    key = f"rank{rank}_step{step}_layer{layer}"
+    if key in audit["captures"] or len(audit["captures"]) >= options.max_captures:
+        return None
+    tensors = [x[:, :options.heads].detach() for x in (q, k, v)]
+    nbytes = sum(x.numel() * x.element_size() for x in tensors)
+    if audit["capture_bytes"] + nbytes > options.max_capture_mib * 1024 ** 2:
+        raise ValueError("capture budget exceeded; capture fewer heads or calls, or raise max-capture-mib")
+    target = Path(options.output_dir) / "captures" / f"{key}.pt"
+    target.parent.mkdir(parents=True, exist_ok=True)
+    metadata = {
+        "model": options.model, "layout": "BNSD", "step": step, "total_steps": steps, "layer": layer,
+        "rank": rank, "scale": scale, "full_shape": list(q.shape), "post_rope": True,
+        "attention_boundary": "post_rope_and_optional_ulysses", "full_kv_context": True, "dtype": str(q.dtype),
+        **options.extra,
+    }
+    torch.save({**dict(zip(("q", "k", "v"), (x.cpu().contiguous() for x in tensors))), "metadata": metadata},
+               target)
+    audit["captures"][key] = str(target.resolve())
+    audit["capture_bytes"] += nbytes
+    return target
 
 
 class ExperimentAdapter:
@@ -80,14 +135,16 @@ class ExperimentAdapter:
 
     ``mode`` is one of ``ARMS``.  ``audit`` is a dict of counters that the
     launcher writes out at exit; ``attention_fn`` defaults to this package's
-    ``attention`` (tests pass a stand-in)."""
+    ``attention`` (tests pass a stand-in); ``capture`` (CaptureOptions) saves
+    the selected calls' Q/K/V before they are attended."""
 
-    def __init__(self, mode, audit=None, *, attention_fn=None):
+    def __init__(self, mode, audit=None, *, attention_fn=None, capture=None):
         if mode not in ARMS:
             raise ValueError(f"mode must be one of {sorted(ARMS)}")
         smooth, cast = ARMS[mode]
         self.mode = mode
         self.audit = _new_audit(mode) if audit is None else audit
+        self.capture_options = capture
         self.vc_config = Config(v_smooth=smooth, expcast=cast)
         self.cache = LayoutCache(self.vc_config)
         self._attention = attention_fn or attention
@@ -128,6 +185,8 @@ class ExperimentAdapter:
         scale = kwargs.get("softmax_scale")
         scale = q4.shape[-1] ** -0.5 if scale is None else scale
         self.audit["calls"] += 1
+        if self.capture_options is not None:
+            capture(self.capture_options, self.audit, q4, k4, v4, step=step, steps=steps, layer=layer, scale=scale)
         out, stats = self._attention(q4, k4, v4, self.vc_config, cache=self.cache, step=step, total_steps=steps,
                                      request_id=self._generation, layer_id=layer, scale=scale)
         self.audit["smoothing_calls"] += int(bool(stats["smoothing_active"]))
@@ -157,14 +216,14 @@ def configure(base):
     return config
 
 
-def register(registry, template, mode, audit):
+def register(registry, template, mode, audit, capture_options=None):
     """Register the adapter class under ``REGISTRY_KEY`` with LightX2V's
     attention registry (``ATTN_WEIGHT_REGISTER``), mixed with its template
     base class (lightx2v.py:203-207)."""
 
     class RegisteredAdapter(ExperimentAdapter, template):
         def __init__(self):
-            ExperimentAdapter.__init__(self, mode, audit)
+            ExperimentAdapter.__init__(self, mode, audit, capture=capture_options)
 
     registry.register(RegisteredAdapter, key=REGISTRY_KEY)
     return RegisteredAdapter
@@ -176,8 +235,25 @@ def main(argv=None):
     parser.add_argument("--output-dir", required=True)
     parser.add_argument("--prepare-only", action="store_true",
                         help="write the patched config and stop (no LightX2V import)")
+    parser.add_argument("--capture", action="store_true",
+                        help="also save post-RoPE Q/K/V of the selected calls under OUTPUT_DIR/captures")
+    parser.add_argument("--capture-steps", type=int, nargs="+", default=[0, 4])
+    parser.add_argument("--capture-layers", type=int, nargs="+", default=[0, 12])
+    parser.add_argument("--capture-rank", type=int, default=0)
+    parser.add_argument("--capture-heads", type=int, default=1)
+    parser.add_argument("--max-captures", type=int, default=4)
+    parser.add_argument("--max-capture-mib", type=int, default=512)
     parser.add_argument("lightx_args", nargs=argparse.REMAINDER)
     options = parser.parse_args(argv)
+    capture_options = None
+    if options.capture:
+        try:
+            capture_options = CaptureOptions(
+                output_dir=options.output_dir, steps=tuple(options.capture_steps),
+                layers=tuple(options.capture_layers), rank=options.capture_rank, heads=options.capture_heads,
+                max_captures=options.max_captures, max_capture_mib=options.max_capture_mib)
+        except ValueError as exc:
+            parser.error(str(exc))
     args = list(options.lightx_args)
     if args[:1] == ["--"]:
         args = args[1:]
@@ -203,7 +279,7 @@ def main(argv=None):
     audit = _new_audit(options.mode)
     audit.update(rank=rank, argv=args, source_config=str(source.resolve()),
                  vc_config=asdict(Config(v_smooth=ARMS[options.mode][0], expcast=ARMS[options.mode][1])))
-    register(ATTN_WEIGHT_REGISTER, AttnWeightTemplate, options.mode, audit)
+    register(ATTN_WEIGHT_REGISTER, AttnWeightTemplate, options.mode, audit, capture_options)
 
     def save_audit():
         (out / f"audit.rank{rank}.json").write_text(json.dumps(audit, indent=2) + "\n", encoding="utf-8")

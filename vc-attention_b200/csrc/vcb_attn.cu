@@ -96,6 +96,7 @@ constexpr float kC2 = 119.6500015258789f;         // 119.65 in fp32
 constexpr float kTwoM24 = 5.9604644775390625e-08f;    // 2^-24
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kMinNormal = 1.17549435e-38f;     // 2^-126
+constexpr uint32_t kParkHintNs = 20000;           // longest park of a parked wait between checks
 
 struct Params {
     CUtensorMap tm_q, tm_k, tm_v, tm_mop;
@@ -233,6 +234,24 @@ struct Waiter {
         store_cluster_u32(peer_abort, 1u);
         return false;
     }
+    // The same wait parked in the barrier between polls (try_wait with a
+    // suspend-time hint): for roles off the critical path, whose polling would
+    // otherwise take issue slots from the softmax and correction warps that
+    // share their SM sub-partition.
+    __device__ __forceinline__ bool parked(uint64_t* bar, uint32_t parity) const {
+        const uint32_t a = smem_u32(bar);
+        if (mbar_try_wait(a, parity)) return true;
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try_wait_sleep(a, parity, kParkHintNs)) {
+            if (*abort) return false;
+            if (globaltimer() - t0 > kWaitLimitNs) {
+                *abort = 1;
+                store_cluster_u32(peer_abort, 1u);
+                return false;
+            }
+        }
+        return true;
+    }
 };
 
 // 2^x as the single MUFU.EX2 instruction, flushing subnormal results to zero.
@@ -278,14 +297,14 @@ __device__ void producer(const Params& p, uint8_t* smem, const Bars& B, const Wa
     for (int it = c; ok && it < p.items; it += ncl, ++li) {
         const int head = it / p.pairs, pair = it - head * p.pairs;
         const int qb = li & 1;
-        if (li >= 2 && !wait(&B.q_free[qb], ((li - 2) >> 1) & 1)) break;
+        if (li >= 2 && !wait.parked(&B.q_free[qb], ((li - 2) >> 1) & 1)) break;
         if (rank == 0) mbar_arrive_expect_tx(&B.q_full[qb], 2 * kQBytes);
         tma_load_3d_pair(smem + kOffQ + qb * kQBytes, &p.tm_q, lead_q + 8 * qb, 0, (2 * pair + (int)rank) * kBM, head);
         q_loaded = li + 1;
         for (int j = 0; j < p.T; ++j, ++g) {
             const int s = g % kStages;
             // stage s last held tile g - kStages: free once its PV is done
-            if (g >= kStages && !wait(&B.o_full[(g - kStages) & 1], ((g - kStages) >> 1) & 1)) {
+            if (g >= kStages && !wait.parked(&B.o_full[(g - kStages) & 1], ((g - kStages) >> 1) & 1)) {
                 ok = false;
                 break;
             }
@@ -324,7 +343,7 @@ __device__ void meta_producer(const Params& p, uint8_t* smem, const Bars& B, con
         const float* meta = p.v_meta + (int64_t)head * p.T * 256;
         for (int j = 0; j < p.T; ++j, ++g) {
             const int s = g % kMetaSlots;
-            if (g >= (uint32_t)kMetaSlots && !wait(&B.meta_empty[s], ((g / kMetaSlots) - 1) & 1)) {
+            if (g >= (uint32_t)kMetaSlots && !wait.parked(&B.meta_empty[s], ((g / kMetaSlots) - 1) & 1)) {
                 ok = false;
                 break;
             }

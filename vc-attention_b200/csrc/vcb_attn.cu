@@ -67,7 +67,7 @@ namespace {
 
 constexpr int kBM = 128;                          // query rows per CTA (256 per pair)
 constexpr int kBN = 128;                          // keys per KV tile
-constexpr int kStages = 4;
+constexpr int kStages = 8;
 constexpr int kMetaSlots = 16;                    // per-tile vscale ring
 constexpr int kThreads = 640;                     // 20 warps: 4 producer/MMA, 8 softmax, 8 correction
 constexpr uint32_t kQBytes = 128 * 128;           // one E4M3 Q tile (16 KB)
@@ -81,7 +81,7 @@ constexpr uint32_t kOffMeta = kOffStages + kStages * kStageBytes;
 constexpr int kStatSlots = 8;                     // per-tile alpha / row-mass ring
 constexpr uint32_t kOffStats = kOffMeta + kMetaSlots * kMetaBytes;  // alpha[8][128], mass[8][128]
 constexpr uint32_t kOffBars = kOffStats + 2 * kStatSlots * 128 * 4;
-constexpr int kNumBars = 2 + 2 + kStages + 2 * kMetaSlots + 4 * 2 + 2 * kStatSlots + 2;
+constexpr int kNumBars = 2 + 2 + 2 * kStages + 2 * kMetaSlots + 4 * 2 + 2 * kStatSlots + 2;
 constexpr uint32_t kOffMisc = kOffBars + kNumBars * 8;
 constexpr uint32_t kSmemBytes = kOffMisc + 16;
 constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;
@@ -122,6 +122,7 @@ struct Bars {
     uint64_t* q_full;      // [2]  even CTA: both Q tiles of an item landed
     uint64_t* q_free;      // [2]  both: the item's QK MMAs are done with Q buffer
     uint64_t* kv_full;     // [kStages]  even CTA: both halves of K / V (/ mean operand) landed
+    uint64_t* kv_empty;    // [kStages]  both: the PV of the stage's tile is done
     uint64_t* meta_full;   // [kMetaSlots]
     uint64_t* meta_empty;  // [kMetaSlots]  the 8 correction warps have read the slot
     uint64_t* s_full;      // [2]  both: QK_g done
@@ -139,6 +140,7 @@ __device__ __forceinline__ Bars bars_at(uint8_t* smem) {
     r.q_full = b; b += 2;
     r.q_free = b; b += 2;
     r.kv_full = b; b += kStages;
+    r.kv_empty = b; b += kStages;
     r.meta_full = b; b += kMetaSlots;
     r.meta_empty = b; b += kMetaSlots;
     r.s_full = b; b += 2;
@@ -224,6 +226,19 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
     }
 }
 
+// Non-blocking check of an mbarrier phase.
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 // A wait that gives up (mbar_wait) and, when it does, raises the peer CTA's
 // abort flag too, so the pair stops together.
 struct Waiter {
@@ -233,6 +248,19 @@ struct Waiter {
         if (mbar_wait(bar, parity, abort)) return true;
         store_cluster_u32(peer_abort, 1u);
         return false;
+    }
+    // Waits for up to three phases.  A barrier check costs a shared-memory
+    // round trip even when the phase is long complete, so the three checks
+    // are issued back to back (non-blocking test_wait) and their latencies
+    // overlap; only a phase found incomplete falls back to the polling wait.
+    // A null barrier is skipped.
+    __device__ __forceinline__ bool all(uint64_t* b0, uint32_t p0, uint64_t* b1, uint32_t p1, uint64_t* b2 = nullptr,
+                                        uint32_t p2 = 0) const {
+        const bool r0 = mbar_test(smem_u32(b0), p0);
+        const bool r1 = !b1 || mbar_test(smem_u32(b1), p1);
+        const bool r2 = !b2 || mbar_test(smem_u32(b2), p2);
+        if (r0 && r1 && r2) return true;
+        return (r0 || (*this)(b0, p0)) && (r1 || (*this)(b1, p1)) && (r2 || (*this)(b2, p2));
     }
     // The same wait parked in the barrier between polls (try_wait with a
     // suspend-time hint): for roles off the critical path, whose polling would
@@ -304,7 +332,7 @@ __device__ void producer(const Params& p, uint8_t* smem, const Bars& B, const Wa
         for (int j = 0; j < p.T; ++j, ++g) {
             const int s = g % kStages;
             // stage s last held tile g - kStages: free once its PV is done
-            if (g >= kStages && !wait.parked(&B.o_full[(g - kStages) & 1], ((g - kStages) >> 1) & 1)) {
+            if (g >= kStages && !wait.parked(&B.kv_empty[s], ((g / kStages) - 1) & 1)) {
                 ok = false;
                 break;
             }
@@ -421,7 +449,7 @@ __device__ __forceinline__ uint64_t smem_desc_k32(const void* p) {
 template <bool HAS_MEAN, uint32_t X>
 __device__ void mma_issuer(const Params& p, uint8_t* smem, const Bars& B, const Waiter& wait, uint32_t tmem, int c,
                            int ncl) {
-    static_assert(kStages == 4, "two issuers with two stages each");
+    static_assert(kStages == 8, "two issuers with four stages each");
     const uint32_t idesc = idesc_e4m3_f32(2 * kBM, kBN);
     const uint32_t idesc_mean = idesc_bf16_f32(2 * kBM, kBN);
     const uint64_t q64 = smem_desc_k128(smem + kOffQ);
@@ -470,22 +498,25 @@ __device__ void mma_issuer(const Params& p, uint8_t* smem, const Bars& B, const 
     }
     auto step = [&](auto S_, uint32_t g) -> bool {
         constexpr uint32_t s = decltype(S_)::value, s2 = (s + 2) % kStages;   // g % kStages
-        if (!wait(&B.p_full[X], (g >> 1) & 1)) return false;
-        if (g >= 2 && !wait(&B.o_free[X], ((g - 2) >> 1) & 1)) return false;
         const bool next = g + 2 < G;
-        if (next && !wait(&B.kv_full[s2], ((g + 2) / kStages) & 1)) return false;
+        if (!wait.all(&B.p_full[X], (g >> 1) & 1, g >= 2 ? &B.o_free[X] : nullptr, ((g - 2) >> 1) & 1,
+                      next ? &B.kv_full[s2] : nullptr, ((g + 2) / kStages) & 1))
+            return false;
         tc_fence_after();
         const uint32_t vlo = k0lo + s * kStageLo + kHalfLo;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) mma2_ts(od, d + (kk >> 1) * 64 + (kk & 1) * 8, vlo + 2 * kk, hi, idesc, kk > 0);
         if (HAS_MEAN) mma2_ts_bf16(od, d + kColMass, m0lo + s * kStageLo, mhi, idesc_mean);
-        commit_both(&B.o_full[X]);       // also frees K/V stage s (the producers wait on it)
+        commit_both(&B.o_full[X]);
+        commit_both(&B.kv_empty[s]);     // the producers may refill stage s
         if (next) return qk(s2);
         return true;
     };
-    for (uint32_t g = X; ok && g < G; g += 4) {
+    for (uint32_t g = X; ok && g < G; g += 8) {
         ok = step(std::integral_constant<uint32_t, X>{}, g);
         if (ok && g + 2 < G) ok = step(std::integral_constant<uint32_t, X + 2>{}, g + 2);
+        if (ok && g + 4 < G) ok = step(std::integral_constant<uint32_t, X + 4>{}, g + 4);
+        if (ok && g + 6 < G) ok = step(std::integral_constant<uint32_t, X + 6>{}, g + 6);
     }
     commit_local_pair(&B.drain[X]);
     drain_wait(&B.drain[X], 0);
@@ -574,7 +605,12 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, cons
                 ++kidx;
             }
             const uint32_t ts = trow + kColS + b * kBN;
-            if (!wait(&B.s_full[b], (g >> 1) & 1)) return;
+            const int slot = g % kStatSlots;
+            // the scores of tile g, and (checked alongside) the statistics
+            // slot this tile writes at its end
+            if (!wait.all(&B.s_full[b], (g >> 1) & 1,
+                          g >= (uint32_t)kStatSlots ? &B.st_free[slot] : nullptr, ((g / kStatSlots) - 1) & 1))
+                return;
             tc_fence_after();
             uint32_t r[64];
             tmem_ld16x2_at<0>(ts, r);
@@ -679,8 +715,6 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, cons
                 const uint32_t w2 = cvt_bf16x2(r2, r1);              // (M2, M3)
                 tmem_st16x2_4_split4(ts + kColMass, hs ? 0u : p1, hs ? 0u : w1, hs ? 0u : w2, 0u);
             }
-            const int slot = g % kStatSlots;
-            if (g >= (uint32_t)kStatSlots && !wait(&B.st_free[slot], ((g / kStatSlots) - 1) & 1)) return;
             if (hs == 0) {
                 st_alpha[slot * 128 + row] = alpha;
                 st_mass[slot * 128 + row] = M;
@@ -713,8 +747,8 @@ __device__ void correction_role(const Params& p, uint8_t* smem, const Bars& B, c
         float den = 0.0f;
         for (int j = 0; j < p.T; ++j, ++g) {
             const uint32_t b = g & 1, slot = g % kStatSlots, s = g % kMetaSlots;
-            if (!wait(&B.o_full[b], (g >> 1) & 1) || !wait(&B.st_full[slot], (g / kStatSlots) & 1) ||
-                !wait(&B.meta_full[s], (g / kMetaSlots) & 1))
+            if (!wait.all(&B.o_full[b], (g >> 1) & 1, &B.st_full[slot], (g / kStatSlots) & 1, &B.meta_full[s],
+                          (g / kMetaSlots) & 1))
                 return;
             tc_fence_after();
             const float alpha = st_alpha[slot * 128 + row];
@@ -810,7 +844,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
             mbar_init(&B.o_full[i], 1);
             mbar_init(&B.o_free[i], 16);          // 8 correction warps in each CTA
         }
-        for (int s = 0; s < kStages; ++s) mbar_init(&B.kv_full[s], 1);
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&B.kv_full[s], 1);
+            mbar_init(&B.kv_empty[s], 1);
+        }
         for (int s = 0; s < kMetaSlots; ++s) {
             mbar_init(&B.meta_full[s], 1);
             mbar_init(&B.meta_empty[s], 8);

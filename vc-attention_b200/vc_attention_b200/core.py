@@ -192,9 +192,11 @@ def attention(
     per call.  By default the call waits for the current stream, reads the
     status word the kernels write, and raises ValueError for non-finite
     Q/K/V (as the reference's isfinite check does) or RuntimeError for an
-    expired device wait.  Given a caller-owned zeroed int32 CUDA tensor of
-    one element, the call only queues the work and ORs its flags into that
-    word; the caller later calls ``b200_backend.raise_for_status(status)``
+    expired device wait.  Given a caller-owned int32 CUDA tensor of one
+    element, the call only queues the work; the word is cleared and then
+    receives this call's flags on the device (use one word per call whose
+    flags must be kept apart); the caller later calls
+    ``b200_backend.raise_for_status(status)``
     and, if it raises, ``counters["rollback"]()`` to put the layout cache
     back as it was before this call."""
     cfg = config or Config()

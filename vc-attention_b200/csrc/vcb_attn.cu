@@ -19,10 +19,12 @@
 //
 // Roles per CTA (640 threads, register budgets rebalanced with setmaxnreg):
 //   warp 0      TMA producer: this CTA's Q tile of each item (2 buffers),
-//               then its halves of K / V / mean-operand tiles into a 4-stage
-//               ring.
-//   warp 1      MMA issuer (even CTA, one thread): S_g = Q8 K8_g^T and
-//               O_g = P_g R_g (+ M_g mu_g), all with cta_group::2.
+//               then its halves of K / V / mean-operand tiles into an
+//               8-stage ring.
+//   warps 1, 3  MMA issuers (even CTA, one thread each; warp 1 takes the
+//               even tiles g and buffers S0 / O0, warp 3 the odd ones and
+//               S1 / O1): S_g = Q8 K8_g^T and O_g = P_g R_g (+ M_g mu_g), all
+//               with cta_group::2.
 //   warp 2      the per-tile V scales into a 16-slot ring.
 //   warps 4-11  softmax, two threads of one warp per query row (64 scores
 //               each): row max, alpha, the ExpCast encode (one packed FMA per
@@ -47,7 +49,7 @@
 // 512 columns).  P_g lives in S_g's columns, so the MMA issues PV_g and then
 // QK_{g+2} into the same buffer (the tensor pipe keeps issue order).  PV_g
 // waits for the correction of tile g - 2 and for K_{g+2}.  The commit that
-// signals PV_g done (o_full, to both CTAs) also frees K/V stage g % 4.
+// signals PV_g done (o_full, to both CTAs) also frees K/V stage g % 8.
 //
 // Numerical contract (core.py:307-341): S = (q8 . k8) * qs * ks * scale;
 // ExpCast code = rne(clamp(fma(S - m, 8 log2 e, 119.65), 0, 120)) viewed as
@@ -554,16 +556,6 @@ __device__ __forceinline__ void tmem_st16x2_16(uint32_t taddr, const uint32_t (&
           "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
         : "memory");
 }
-// 32 lanes x 16 consecutive 32-bit columns; thread i of the warp gets lane i
-__device__ __forceinline__ void tmem_ld32x16(uint32_t taddr, uint32_t (&r)[16]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-}
-
 // thread t < 16: lane base + t, columns [c, c + 4); thread t + 16: the same
 // lane, columns [c + 4, c + 8): one row's 8 consecutive columns from the pair
 __device__ __forceinline__ void tmem_st16x2_4_split4(uint32_t taddr, uint32_t a, uint32_t b, uint32_t c,

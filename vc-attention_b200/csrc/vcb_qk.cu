@@ -193,24 +193,15 @@ __device__ __forceinline__ void transform_half(const RowArgs& a, int64_t h, int6
 // stride 2 on, the stride-64 exchange and the normalisation are add / fma /
 // mul .f32x2, each lane rounded once like the scalar form.  l - r is computed
 // as fma(r, -1, l): the product is exact, so the result is RN(l - r) with the
-// same sign of zero.
-template <typename T>
-__device__ __forceinline__ void transform_half128(const RowArgs& a, int64_t h, int64_t tok, bool valid, int half,
-                                                  const float* smean, float2 (&x)[32]) {
+// same sign of zero.  hadamard_half128 takes the half row already in x
+// (zeros for an invalid row); transform_half128 loads it from global memory.
+__device__ __forceinline__ void hadamard_half128(bool valid, int half, const float* smean, float2 (&x)[32]) {
     const int c0 = 64 * half;
     const float2 neg1 = make_float2(-1.0f, -1.0f);
-    if (valid) {
-        const T* src = static_cast<const T*>(a.x) + (h * a.S + tok) * 128 + c0;
+    if (valid && smean) {
+        const float2* m2 = reinterpret_cast<const float2*>(smean + c0);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) load8x2(src + 8 * i, x + 4 * i);
-        if (smean) {
-            const float2* m2 = reinterpret_cast<const float2*>(smean + c0);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) x[i] = ffma2(m2[i], neg1, x[i]);
-        }
-    } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) x[i] = make_float2(0.0f, 0.0f);
+        for (int i = 0; i < 32; ++i) x[i] = ffma2(m2[i], neg1, x[i]);
     }
 #pragma unroll
     for (int i = 0; i < 32; ++i) {          // stride 1: inside one pair
@@ -242,6 +233,20 @@ __device__ __forceinline__ void transform_half128(const RowArgs& a, int64_t h, i
     const float2 norm2 = make_float2(0.08838834764831845f, 0.08838834764831845f);   // fp32(128^-0.5)
 #pragma unroll
     for (int i = 0; i < 32; ++i) x[i] = fmul2(x[i], norm2);
+}
+
+template <typename T>
+__device__ __forceinline__ void transform_half128(const RowArgs& a, int64_t h, int64_t tok, bool valid, int half,
+                                                  const float* smean, float2 (&x)[32]) {
+    if (valid) {
+        const T* src = static_cast<const T*>(a.x) + (h * a.S + tok) * 128 + 64 * half;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) load8x2(src + 8 * i, x + 4 * i);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) x[i] = make_float2(0.0f, 0.0f);
+    }
+    hadamard_half128(valid, half, smean, x);
 }
 
 // 64 E4M3 bytes of a half row: x / scale as div_by(x * pre, bdiv, rdiv)
@@ -389,6 +394,130 @@ __global__ void __launch_bounds__(512) qk_quant_kernel(RowArgs a) {
     }
 }
 
+// ------------------------------------------------------------------------
+// Persistent, staged form of qk_quant_kernel for 16-bit rows with D == 128,
+// the 128-point Hadamard and blocks of 16 to 256 rows that divide 256 (a
+// block spans whole warps; every Q block of the b200 configurations and K
+// blocks up to 256).  The unstaged kernel holds one block's rows in
+// registers from load to encode, so an SM has only one or two blocks' loads
+// in flight and HBM idles while they compute.  Here one CTA of 16 warps per
+// SM walks 256-row slabs (slab = one K block or several Q blocks), two
+// threads per row as in qk_quant_kernel.  Each thread copies its own half
+// row of the slab two steps ahead into a 3-slot shared-memory ring with
+// 16-byte cp.async copies (through the permutation for K), so two slabs'
+// loads are in flight while a third is transformed, and it reads back only
+// what it copied itself: no barrier guards the ring.  Transform, block
+// maximum and encode are qk_quant_kernel's, bit for bit.  Rows sit 272 bytes
+// apart so that the 16 rows a warp reads at one column offset fall in
+// different banks.
+constexpr int kSlabRows = 256;
+constexpr int kSlabStages = 3;
+constexpr uint32_t kSlabPitch = 272;                              // bytes per staged row (256 + 16)
+constexpr uint32_t kSlabStageBytes = kSlabRows * kSlabPitch;      // 69632
+constexpr int kStagedWarps = 16;
+constexpr int kStagedThreads = kStagedWarps * 32;
+constexpr uint32_t kStagedSmem = kSlabStages * kSlabStageBytes + 2 * kStagedWarps * 4;
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// eight 16-bit elements from shared memory as four channel pairs
+template <typename T>
+__device__ __forceinline__ void lds8x2(uint32_t addr, float2* o) {
+    uint32_t w[4];
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3])
+                 : "r"(addr)
+                 : "memory");
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        if constexpr (std::is_same<T, __nv_bfloat16>::value)
+            o[i] = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+        else
+            o[i] = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+    }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kStagedThreads, 1) qk_quant_staged_kernel(RowArgs a, int64_t slabs_per_head,
+                                                                            int64_t nslabs) {
+    extern __shared__ __align__(128) uint8_t sm[];
+    float* partial = reinterpret_cast<float*>(sm + kSlabStages * kSlabStageBytes);   // [2][kStagedWarps]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int half = lane >> 4;
+    const int rl = warp * 16 + (lane & 15);               // row in the slab
+    const int B = a.block;                                // a multiple of 16 dividing kSlabRows
+    const int w0 = (rl / B) * B / 16, w1 = w0 + B / 16;   // the warps of this row's block
+    const T* x = static_cast<const T*>(a.x);
+    const uint32_t slot0 = smem_u32(sm) + (uint32_t)rl * kSlabPitch + 128u * half;
+    // this thread's half row of slab `slab` into ring slot `s` (nothing past S)
+    auto fetch = [&](int64_t slab, int s) {
+        if (slab < nslabs) {
+            const int64_t h = slab / slabs_per_head, r = (slab % slabs_per_head) * kSlabRows + rl;
+            if (r < a.S) {
+                const int64_t tok = a.pi ? (int64_t)a.pi[h * a.S + r] : r;
+                const T* src = x + (h * a.S + tok) * 128 + 64 * half;
+                const uint32_t dst = slot0 + (uint32_t)s * kSlabStageBytes;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) cp_async16(dst + 16u * i, src + 8 * i);
+            }
+        }
+        cp_async_commit();                               // one group per step, empty or not
+    };
+    fetch(blockIdx.x, 0);
+    fetch(blockIdx.x + gridDim.x, 1);
+    int it = 0;
+    for (int64_t slab = blockIdx.x; slab < nslabs; slab += gridDim.x, ++it) {
+        const int s = it % kSlabStages;
+        fetch(slab + 2 * (int64_t)gridDim.x, (it + 2) % kSlabStages);
+        cp_async_wait<2>();                              // this thread's copies of `slab` have landed
+        const int64_t h = slab / slabs_per_head, r0 = (slab % slabs_per_head) * kSlabRows;
+        const int64_t r = r0 + rl;
+        const bool valid = r < a.S;
+        float2 xv[32];
+        if (valid) {
+            const uint32_t row = slot0 + (uint32_t)s * kSlabStageBytes;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) lds8x2<T>(row + 16u * i, xv + 4 * i);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) xv[i] = make_float2(0.0f, 0.0f);
+        }
+        hadamard_half128(valid, half, a.mean ? a.mean + h * 128 : nullptr, xv);
+        float amax = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) amax = fmax3_nan(amax, fabsf(xv[i].x), fabsf(xv[i].y));
+        for (int o = 16; o > 0; o >>= 1) amax = fmax_nan(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        if (lane == 0) partial[(it & 1) * kStagedWarps + warp] = amax;
+        __syncthreads();
+        float bmax = 0.0f;
+        for (int w = w0; w < w1; ++w) bmax = fmax_nan(bmax, partial[(it & 1) * kStagedWarps + w]);
+        float scale = bmax / 448.0f;
+        if (scale == 0.0f) scale = 1.0f;
+        const int64_t b = r / B;
+        if (rl % B == 0 && half == 0 && r < a.S_pad) {
+            if (!finite_f(bmax)) flag_status(a.status, VCB_FLAG_NONFINITE);
+            if (b < a.nblk) a.scales[h * a.nblk + b] = scale;
+        }
+        if (r >= a.S_pad) continue;
+        uint4* dst = reinterpret_cast<uint4*>(a.payload + (h * a.S_pad + r) * 128 + 64 * half);
+        if (!valid) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) dst[q] = make_uint4(0u, 0u, 0u, 0u);
+            continue;
+        }
+        const float pre = div_prescale(scale);
+        const float bdiv = scale * pre, rdiv = __frcp_rn(scale * pre);
+        if (pre == 1.0f) encode_half128<false>(xv, pre, bdiv, rdiv, dst);   // block-uniform
+        else encode_half128<true>(xv, pre, bdiv, rdiv, dst);
+    }
+    cp_async_wait<0>();                                  // nothing lands after the CTA exits
+}
+
 // Transform-only rows (the preprocess_qk export): one row per thread.
 template <typename T>
 __global__ void __launch_bounds__(128) qk_transform_kernel(RowArgs a) {
@@ -428,8 +557,34 @@ int launch_k_mean(const void* k, int64_t heads, int64_t S, int D, float* partial
     return VCB_OK;
 }
 
+// SMs of the current device, looked up once per device
+int sm_count() {
+    static int cache[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (cache[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n < 1) n = 148;
+        cache[dev] = n;
+    }
+    return cache[dev];
+}
+
 template <typename T>
 int launch_rows(const RowArgs& a, int64_t heads, bool quantise, cudaStream_t st) {
+    constexpr bool k16 = std::is_same<T, __nv_bfloat16>::value || std::is_same<T, __half>::value;
+    const bool aligned = (reinterpret_cast<uintptr_t>(a.x) & 15u) == 0 &&
+                         (reinterpret_cast<uintptr_t>(a.mean) & 15u) == 0;
+    if (k16 && quantise && a.D == 128 && a.hadamard && a.block % 16 == 0 && kSlabRows % a.block == 0 && aligned) {
+        const int64_t slabs_per_head = (a.S_pad + kSlabRows - 1) / kSlabRows;
+        const int64_t nslabs = heads * slabs_per_head;
+        const int64_t grid = nslabs < sm_count() ? nslabs : sm_count();
+        auto kernel = qk_quant_staged_kernel<T>;
+        VCB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kStagedSmem));
+        kernel<<<(unsigned)grid, kStagedThreads, kStagedSmem, st>>>(a, slabs_per_head, nslabs);
+        VCB_CUDA(cudaGetLastError());
+        return VCB_OK;
+    }
     if (quantise) {
         const unsigned grid = (unsigned)(a.S_pad / a.block);
         const int rows = a.block < 256 ? a.block : 256;

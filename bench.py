@@ -36,6 +36,7 @@ Other cases (not the bench line):
 from __future__ import annotations
 
 import argparse
+import gc
 import json
 import os
 import pathlib
@@ -448,6 +449,10 @@ def run_ours(args, world, rank, local):
     hout = torch.empty(q.shape, dtype=q.dtype).pin_memory()
     barrier(world)
     e2e_ms, e2e_stats = [], []
+    # the host issues every chunk's copies and launches inside the timed
+    # region, so a garbage-collector pause there would stall the GPU
+    gc.collect()
+    gc.disable()
     for i in range(args.warmup + args.steps):
         torch.cuda.synchronize()
         barrier(world)
@@ -461,6 +466,7 @@ def run_ours(args, world, rank, local):
         e2e_stats.append(st)
         if i >= args.warmup:
             e2e_ms.append(s.elapsed_time(e))
+    gc.enable()
     # every e2e step's device status is read after the timed loop: a step
     # whose kernels flagged non-finite input, an expired wait or a failed
     # layout check invalidates the e2e figure (check_streamed raises)

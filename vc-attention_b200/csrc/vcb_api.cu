@@ -119,6 +119,22 @@ int check_attn(const vcb_attn_args* a) {
 
 using namespace vcb;
 
+namespace vcb {
+// SMs of the current device, looked up once per device (148 when the
+// lookup fails: the value only sizes persistent grids)
+int sm_count() {
+    static int cache[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (cache[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n < 1) n = 148;
+        cache[dev] = n;
+    }
+    return cache[dev];
+}
+}  // namespace vcb
+
 extern "C" {
 
 int vcb_abi_version(void) { return VCB_ABI_VERSION; }

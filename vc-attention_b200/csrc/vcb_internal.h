@@ -17,6 +17,7 @@ size_t group_workspace_bytes(int64_t heads, int64_t s, int d, int clusters);
 int group_run(const vcb_group_args* p, cudaStream_t st);
 
 // vcb_attn.cu
+int sm_count();
 int attn_run(const vcb_attn_args* p, const vcb_attn_probe* probe, cudaStream_t st);
 int wait_selftest_run(int complete, const void* src, int32_t* status, int32_t* report, cudaStream_t st);
 

@@ -557,19 +557,6 @@ int launch_k_mean(const void* k, int64_t heads, int64_t S, int D, float* partial
     return VCB_OK;
 }
 
-// SMs of the current device, looked up once per device
-int sm_count() {
-    static int cache[64] = {};
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-    if (cache[dev] == 0) {
-        int n = 0;
-        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n < 1) n = 148;
-        cache[dev] = n;
-    }
-    return cache[dev];
-}
-
 template <typename T>
 int launch_rows(const RowArgs& a, int64_t heads, bool quantise, cudaStream_t st) {
     constexpr bool k16 = std::is_same<T, __nv_bfloat16>::value || std::is_same<T, __half>::value;

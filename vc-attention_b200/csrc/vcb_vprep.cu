@@ -26,6 +26,13 @@ __device__ __forceinline__ float to_float(float x) { return x; }
 __device__ __forceinline__ float to_float(__half x) { return __half2float(x); }
 __device__ __forceinline__ float to_float(__nv_bfloat16 x) { return __bfloat162float(x); }
 
+// three-input min that returns NaN when any input is NaN (sm_100)
+__device__ __forceinline__ float fmin3_nan(float a, float b, float c) {
+    float d;
+    asm("min.NaN.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
 template <typename T>
 __global__ void __launch_bounds__(128) vprep_kernel(const T* __restrict__ v, int64_t S, int dv,
                                                     const int32_t* __restrict__ pi, int active,
@@ -84,17 +91,21 @@ __global__ void __launch_bounds__(128) vprep_kernel(const T* __restrict__ v, int
         float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};
         float xmax = -INFINITY, xmin = INFINITY;
         if (cnt == kTile) {
+            // tokens in pairs: part j % 4 in packed adds (each lane the same
+            // RN add in token order); max.NaN / min.NaN carry a NaN or an
+            // infinity to xmax / xmin, which is then the finiteness check
+            float2 p01 = make_float2(0.0f, 0.0f), p23 = make_float2(0.0f, 0.0f);
 #pragma unroll 8
             for (int j = 0; j < kTile; j += 4) {
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float x = to_float(tile[(j + e) * 128 + c]);
-                    ok &= finite_f(x);
-                    part[e] += x;
-                    xmax = fmaxf(xmax, x);
-                    xmin = fminf(xmin, x);
-                }
+                const float x0 = to_float(tile[j * 128 + c]), x1 = to_float(tile[(j + 1) * 128 + c]);
+                const float x2 = to_float(tile[(j + 2) * 128 + c]), x3 = to_float(tile[(j + 3) * 128 + c]);
+                p01 = fadd2(p01, make_float2(x0, x1));
+                p23 = fadd2(p23, make_float2(x2, x3));
+                xmax = fmax3_nan(fmax3_nan(xmax, x0, x1), x2, x3);
+                xmin = fmin3_nan(fmin3_nan(xmin, x0, x1), x2, x3);
             }
+            ok = finite_f(xmax) && finite_f(xmin);
+            part[0] = p01.x; part[1] = p01.y; part[2] = p23.x; part[3] = p23.y;
         } else {
             for (int j = 0; j < cnt; ++j) {
                 const float x = to_float(tile[j * 128 + c]);
@@ -115,16 +126,39 @@ __global__ void __launch_bounds__(128) vprep_kernel(const T* __restrict__ v, int
         const float pre = div_prescale(scale);
         const float bdiv = scale * pre;
         const float rdiv = __frcp_rn(bdiv);
+        if (cnt == kTile) {
+            // div_by on token pairs in packed FP32 (fma(q, -b, x) is
+            // fma(-q, b, x): the same exact product); a unit prescale is
+            // skipped, which changes nothing
+            const float2 nm = make_float2(-mean, -mean), p2 = make_float2(pre, pre);
+            const float2 y2 = make_float2(rdiv, rdiv), nb2 = make_float2(-bdiv, -bdiv);
 #pragma unroll
-        for (int w = 0; w < 32; ++w) {
-            float q[4];
+            for (int w = 0; w < 32; ++w) {
+                uint32_t b2[2];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int j = 4 * w + e;
-                const float r = to_float(tile[j * 128 + c]) - mean;
-                q[e] = j < cnt ? div_by(__fmul_rn(r, pre), bdiv, rdiv) : 0.0f;
+                for (int e = 0; e < 2; ++e) {
+                    const int j = 4 * w + 2 * e;
+                    float2 r = fadd2(make_float2(to_float(tile[j * 128 + c]), to_float(tile[(j + 1) * 128 + c])), nm);
+                    if (pre != 1.0f) r = fmul2(r, p2);
+                    const float2 qq = fmul2(r, y2);
+                    const float2 rr = ffma2(qq, nb2, r);
+                    const float2 d = ffma2(rr, y2, qq);
+                    b2[e] = e4m3x2(d.x, d.y);
+                }
+                packed[w] = b2[0] | (b2[1] << 16);
             }
-            packed[w] = e4m3x2(q[0], q[1]) | (e4m3x2(q[2], q[3]) << 16);
+        } else {
+#pragma unroll
+            for (int w = 0; w < 32; ++w) {
+                float q[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int j = 4 * w + e;
+                    const float r = to_float(tile[j * 128 + c]) - mean;
+                    q[e] = j < cnt ? div_by(__fmul_rn(r, pre), bdiv, rdiv) : 0.0f;
+                }
+                packed[w] = e4m3x2(q[0], q[1]) | (e4m3x2(q[2], q[3]) << 16);
+            }
         }
         const float sm = __fdiv_rn(mean, scale);
         stored = mean_type == 1 ? __half2float(__float2half_rn(sm))

@@ -493,7 +493,12 @@ __global__ void __launch_bounds__(kStagedThreads, 1) qk_quant_staged_kernel(RowA
         for (int i = 0; i < 32; ++i) amax = fmax3_nan(amax, fabsf(xv[i].x), fabsf(xv[i].y));
         for (int o = 16; o > 0; o >>= 1) amax = fmax_nan(amax, __shfl_xor_sync(0xffffffffu, amax, o));
         if (lane == 0) partial[(it & 1) * kStagedWarps + warp] = amax;
-        __syncthreads();
+        // only the B / 16 warps of this row's block meet, so the blocks of a
+        // slab drift apart and overlap their latencies (one warp for B = 16;
+        // named barrier 1 + block index, 2 B threads, for B = 32 .. 128)
+        if (B == 16) __syncwarp();
+        else if (B == kSlabRows) __syncthreads();
+        else asm volatile("bar.sync %0, %1;" ::"r"(1 + rl / B), "r"(2 * B) : "memory");
         float bmax = 0.0f;
         for (int w = w0; w < w1; ++w) bmax = fmax_nan(bmax, partial[(it & 1) * kStagedWarps + w]);
         float scale = bmax / 448.0f;

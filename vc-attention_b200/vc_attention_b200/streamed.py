@@ -60,7 +60,7 @@ def attention_streamed(q, k, v, config=None, *, cache=None, step=0, total_steps=
     host, stats).  Pinned inputs (``tensor.pin_memory()``) let the copies
     overlap the compute; ``out`` may be a preallocated pinned host tensor.
     ``chunk_heads`` sets how many of the B*H heads go through the pipeline
-    at a time (default: a fortieth of them, at least one).  With
+    at a time (default: a twentieth of them, at least one).  With
     ``synchronize=False`` the call returns once the work is queued (the
     output is complete when the device's current stream reaches this point)
     and does not read the device status word.  The caller then owns that
@@ -85,7 +85,7 @@ def attention_streamed(q, k, v, config=None, *, cache=None, step=0, total_steps=
     elif out.shape != (b, h, sq, dv) or out.dtype != q.dtype or out.device.type != "cpu":
         raise ValueError("out must be a host tensor of the output's shape and dtype")
     of = out.view(bh, sq, dv)
-    size = chunk_heads or max(1, math.ceil(bh / 40))
+    size = chunk_heads or max(1, math.ceil(bh / 20))
     parts = _chunks(bh, size)
     if cache is None:
         cache = LayoutCache(cfg)

@@ -38,6 +38,7 @@ from __future__ import annotations
 import argparse
 import gc
 import json
+import math
 import os
 import pathlib
 import statistics
@@ -291,6 +292,52 @@ def copy_ceiling_ms(hq, hk, hv, hout, device, reps=3):
     return best
 
 
+def chunked_copy_ceiling_ms(hq, hk, hv, hout, device, reps=3, nbuf=8):
+    """The e2e pipeline's copy traffic alone: per chunk of heads (the
+    default of attention_streamed, a twentieth of them) three H2D copies
+    into a ring of `nbuf` device slots on one stream, and one D2H copy of a
+    chunk-sized slot on another once that chunk has landed, a slot reused
+    once its D2H is done.  Both directions then carry many mid-sized copies
+    at once, as in the pipeline, which the link serves more slowly than one
+    copy per direction."""
+    bh = hq.shape[0] * hq.shape[1]
+    size = max(1, math.ceil(bh / 20))
+    parts = [(a, min(a + size, bh)) for a in range(0, bh, size)]
+    nbuf = min(nbuf, len(parts))
+    flat = [x.reshape(bh, x.shape[2], x.shape[3]) for x in (hq, hk, hv)]
+    of = hout.reshape(bh, hout.shape[2], hout.shape[3])
+    ring = [torch.empty((nbuf, size) + tuple(x.shape[1:]), dtype=x.dtype, device=device) for x in flat]
+    up, down = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    best = float("inf")
+    for _ in range(reps):
+        torch.cuda.synchronize(device)
+        ready = [torch.cuda.Event() for _ in parts]
+        free = [torch.cuda.Event() for _ in parts]
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        cur = torch.cuda.current_stream(device)
+        s.record(cur)
+        up.wait_stream(cur)
+        down.wait_stream(cur)
+        for i, (a, b_) in enumerate(parts):
+            slot, m = i % nbuf, b_ - a
+            with torch.cuda.stream(up):
+                if i >= nbuf:
+                    up.wait_event(free[i - nbuf])
+                for r, x in zip(ring, flat):
+                    r[slot, :m].copy_(x[a:b_], non_blocking=True)
+                ready[i].record(up)
+            with torch.cuda.stream(down):
+                down.wait_event(ready[i])
+                of[a:b_].copy_(ring[0][slot, :m], non_blocking=True)
+                free[i].record(down)
+        cur.wait_stream(up)
+        cur.wait_stream(down)
+        e.record(cur)
+        e.synchronize()
+        best = min(best, s.elapsed_time(e))
+    return best
+
+
 def config4_object(args, world, rank, local):
     """Configuration 4 inside the multi-GPU bench line: B1 H24 S131072 D128
     bf16, combined mode at a refresh step, inputs sequence-sharded (S/N tokens
@@ -474,6 +521,7 @@ def run_ours(args, world, rank, local):
         check_streamed(st)
     e2e = sharding.max_over_ranks(sum(e2e_ms) / len(e2e_ms))
     ceiling = sharding.max_over_ranks(copy_ceiling_ms(hq, hk, hv, hout, device))
+    ceiling_chunked = sharding.max_over_ranks(chunked_copy_ceiling_ms(hq, hk, hv, hout, device))
     c4 = config4_object(args, world, rank, local) if world > 1 and not args.no_config4 else None
 
     cpu = None
@@ -497,7 +545,12 @@ def run_ours(args, world, rank, local):
                     "copy_ceiling_ms": ceiling,
                     "frac_of_copy_ceiling": ceiling / e2e,
                     "copy_ceiling": "the same H2D and D2H bytes alone, pinned, one stream per direction, "
-                                    "max over ranks"},
+                                    "max over ranks",
+                    "copy_ceiling_chunked_ms": ceiling_chunked,
+                    "frac_of_chunked_copy_ceiling": ceiling_chunked / e2e,
+                    "copy_ceiling_chunked": "the pipeline's own copies alone: per chunk of heads three H2D "
+                                            "copies into a ring of 8 device slots and one chunk-sized D2H, "
+                                            "the two directions at once, max over ranks"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": traffic, "traffic_source": traffic_note,
                          "kernel": "attn_kernel",

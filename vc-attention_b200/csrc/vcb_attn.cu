@@ -9,57 +9,54 @@
 // rank r of the pair owns query tile 2p + r of a head (128 rows), and the
 // pair's MMAs are tcgen05.mma.cta_group::2 with M = 256: one instruction,
 // issued by one thread of the even CTA, multiplies both CTAs' rows.  Each CTA
-// loads only its half of every K tile (64 keys), V tile (64 channels) and
-// mean-operand tile, with ordinary (non-multicast) TMA loads that report to
-// the even CTA's barrier.  The grid holds as many pairs as fit on the GPU at
-// once, and each pair walks the (head, pair-of-query-tiles) items
+// loads only its half of every K tile (64 keys) and its share of every V tile
+// (channels 0..71 or 72..127), with ordinary (non-multicast) TMA loads that
+// report to the even CTA's barrier.  The grid holds as many pairs as fit on
+// the GPU at once, and each pair walks the (head, pair-of-query-tiles) items
 // c, c + clusters, ... in order, so the K/V of one or two heads are in L2 at
 // a time.  Barrier phases run on across items; the prologue and epilogue of
 // consecutive items overlap.
 //
 // Roles per CTA (640 threads, register budgets rebalanced with setmaxnreg):
 //   warp 0      TMA producer: this CTA's Q tile of each item (2 buffers),
-//               then its halves of K / V / mean-operand tiles into an
-//               8-stage ring.
+//               then its share of K / V tiles into an 8-stage ring.
 //   warps 1, 3  MMA issuers (even CTA, one thread each; warp 1 takes the
-//               even tiles g and buffers S0 / O0, warp 3 the odd ones and
-//               S1 / O1): S_g = Q8 K8_g^T and O_g = P_g R_g (+ M_g mu_g), all
-//               with cta_group::2.
-//   warp 2      the per-tile V scales into a 16-slot ring.
+//               even tiles g and buffer S0, warp 3 the odd ones and S1):
+//               S_g = Q8 K8_g^T and O = P_g [V8_g | 1], all with
+//               cta_group::2.
+//   warp 2      the per-tile V scales and stored means into a 16-slot ring.
 //   warps 4-11  softmax, two threads of one warp per query row (64 scores
 //               each): row max, alpha, the ExpCast encode (one packed FMA per
 //               pair of scores; the f16-subnormal conversion rounds to the
-//               integer code and clamps it at zero) or exp + E4M3(p * 256),
-//               the row mass; P_g back over its own S_g columns, and with
-//               V-Smooth the row mass as three bf16 pieces beside it.
+//               integer code and clamps it at zero) or exp + E4M3(p * 256)
+//               with its FP32 row mass; P_g back over its own S_g columns.
 //   warps 12-19 correction, two threads per row (64 channels each):
-//               acc = alpha acc + O_g vscale_g, den = alpha den + M_g;
+//               acc = alpha acc + (O + M mu) vscale, den = alpha den + M;
 //               epilogue acc / den in the output dtype after each item.
 //
-// V-mean recovery on the tensor core.  The reference adds rowmass * mu_g to
-// PV / 256 before scaling by vscale_g (core.py:334).  Here one extra MMA of
-// kind::f16 (K = 16, bf16 operands) adds M_g mu_g into O_g: A is the row
-// mass split into bf16 pieces M1 + M2 + M3, B the stored mean mu / vscale
-// split into u1 + u2 + u3 (written by the V tile kernel), and the K slots
-// hold the six products Mi uj with i + j <= 4, which carry the FP32 product
-// to about 2^-24.  The correction then does one packed FMA per two channels
-// instead of two, and reads no means.
+// Row mass on the tensor core.  The PV MMA has N = 144: the odd CTA's B rows
+// 56..71 of every stage hold E4M3 ones, so O columns 128..143 each receive
+// sum(P) of the row, the ExpCast row mass of decoded probabilities
+// (core.py:330-332), from the same products as PV.  The softmax then only
+// encodes.  The exp mode's row mass is the FP32 sum of unrounded
+// probabilities, which the softmax keeps computing.
 //
-// Latency hiding: S and O are double-buffered in TMEM (S0, S1, O0, O1 use all
-// 512 columns).  P_g lives in S_g's columns, so the MMA issues PV_g and then
-// QK_{g+2} into the same buffer (the tensor pipe keeps issue order).  PV_g
-// waits for the correction of tile g - 2 and for K_{g+2}.  The commit that
-// signals PV_g done (o_full, to both CTAs) also frees K/V stage g % 8.
+// Latency hiding: S is double-buffered in TMEM (S0, S1, then O with its mass
+// columns: 400 of 512 columns).  P_g lives in S_g's columns, so the MMA issues
+// PV_g and then QK_{g+2} into the same buffer (the tensor pipe keeps issue
+// order).  PV_g waits for the corrections' read of O_{g-1} and for K_{g+2}.
+// The commit that signals PV_g done (o_full, to both CTAs) also frees K/V
+// stage g % 8.
 //
 // Numerical contract (core.py:307-341): S = (q8 . k8) * qs * ks * scale;
 // ExpCast code = rne(clamp(fma(S - m, 8 log2 e, 119.65), 0, 120)) viewed as
 // E4M3 with a 1/256 scale, row mass = sum of decoded P; non-ExpCast P8 =
-// e4m3(exp(S - m) * 256) with an FP32 row mass of exp; V-mean recovery lives
-// inside the accumulator and is rescaled with the running max.  The
-// accumulators are kept in units of 256 (acc256 = 256 acc, den256 = 256
-// den); 256 is a power of two, so no rounding changes.  Every mbarrier wait
-// is bounded (vcb_common.cuh); a CTA that gives up tells its peer, and the
-// pair drains and frees its tensor memory together.
+// e4m3(exp(S - m) * 256) with an FP32 row mass of exp; V-mean recovery adds
+// rowmass * mu / vscale to PV before the scale and is rescaled with the
+// running max.  The accumulators are kept in units of 256 (acc256 = 256 acc,
+// den256 = 256 den); 256 is a power of two, so no rounding changes.  Every
+// mbarrier wait is bounded (vcb_common.cuh); a CTA that gives up tells its
+// peer, and the pair drains and frees its tensor memory together.
 #include "vcb_internal.h"
 #include <type_traits>
 
@@ -73,25 +70,38 @@ constexpr int kStages = 8;
 constexpr int kMetaSlots = 16;                    // per-tile vscale ring
 constexpr int kThreads = 640;                     // 20 warps: 4 producer/MMA, 8 softmax, 8 correction
 constexpr uint32_t kQBytes = 128 * 128;           // one E4M3 Q tile (16 KB)
-constexpr uint32_t kHalf = 64 * 128;              // this CTA's half of a K or V tile (8 KB)
-constexpr uint32_t kMopHalf = 64 * 32;            // this CTA's half of a mean-operand tile (2 KB)
-constexpr uint32_t kStageBytes = 2 * kHalf + kMopHalf;   // 18 KB, a multiple of 1024
+constexpr uint32_t kHalf = 64 * 128;              // this CTA's half of a K tile (8 KB)
+// The PV MMA's B operand.  ExpCast: 72 rows of 128 keys in each CTA (N =
+// 144); the even CTA loads V channels 0..71, the odd CTA channels 72..127
+// into rows 0..55 and keeps E4M3 ones in rows 56..71, so O columns 0..127 are
+// the 128 channels in order and columns 128..143 each hold the row mass
+// sum(P).  The exp mode (its row mass is the FP32 sum of unrounded
+// probabilities, which the softmax forms) loads 64 channels per CTA, N = 128.
+constexpr int kVRows0 = 72, kVRows1 = 56;         // V channels loaded by the even / odd CTA (ExpCast)
+constexpr uint32_t kVBytes = 72 * 128;            // one CTA's B rows of a stage (9 KB)
+constexpr uint32_t kStageBytes = kHalf + kVBytes; // 17 KB, a multiple of 1024
 constexpr uint32_t kOffQ = 0;                     // Q buffers 0, 1
 constexpr uint32_t kOffStages = 2 * kQBytes;
-constexpr uint32_t kMetaBytes = 512;              // vscale[128]
+constexpr uint32_t kMetaBytes = 1024;             // vscale[128], stored mean mu / vscale [128]
 constexpr uint32_t kOffMeta = kOffStages + kStages * kStageBytes;
 constexpr int kStatSlots = 8;                     // per-tile alpha / row-mass ring
 constexpr uint32_t kOffStats = kOffMeta + kMetaSlots * kMetaBytes;  // alpha[8][128], mass[8][128]
 constexpr uint32_t kOffBars = kOffStats + 2 * kStatSlots * 128 * 4;
-constexpr int kNumBars = 2 + 2 + 2 * kStages + 2 * kMetaSlots + 4 * 2 + 2 * kStatSlots + 2;
+constexpr int kNumBars = 2 + 2 + 2 * kStages + 2 * kMetaSlots + 5 * 2 + 2 * kStatSlots + 2;
 constexpr uint32_t kOffMisc = kOffBars + kNumBars * 8;
 constexpr uint32_t kSmemBytes = kOffMisc + 16;
 constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS = 0;                     // S0, S1 (P and the row-mass pieces inside)
-constexpr uint32_t kColO = 256;                   // O0, O1
-constexpr uint32_t kColMass = 16;                 // row-mass operand: S_b columns [16, 24)
+// Tensor memory: one S buffer, and two of P (the E4M3 codes, 4 per column)
+// and O (128 channels, then 16 columns of row mass).  The D operands sit at
+// multiples of 64 columns.
+constexpr uint32_t kColS = 0;
+constexpr uint32_t kColO0 = 128, kColO1 = 320;
+constexpr uint32_t kColP0 = 272, kColP1 = 464;
+constexpr uint32_t kColMass = 128;                // the row-mass column inside O_b
+constexpr int kPvN = 144;                         // N of the PV MMA with the row-mass columns
 static_assert(kStageBytes % 1024 == 0, "swizzled tiles need 1024-byte aligned stages");
+static_assert(kVRows0 + kVRows1 == 128 && kVRows1 % 8 == 0 && 2 * kVRows0 == kPvN, "V split");
 
 constexpr float kC1 = 11.541560173034668f;        // 8 log2(e) in fp32
 constexpr float kC2 = 119.6500015258789f;         // 119.65 in fp32
@@ -101,7 +111,7 @@ constexpr float kMinNormal = 1.17549435e-38f;     // 2^-126
 constexpr uint32_t kParkHintNs = 20000;           // longest park of a parked wait between checks
 
 struct Params {
-    CUtensorMap tm_q, tm_k, tm_v, tm_mop;
+    CUtensorMap tm_q, tm_k, tm_v0, tm_v1;      // V boxes of kVRows0 / kVRows1 channel rows
     const float* q_scale;
     const float* k_scale;
     const float* v_meta;
@@ -127,10 +137,11 @@ struct Bars {
     uint64_t* kv_empty;    // [kStages]  both: the PV of the stage's tile is done
     uint64_t* meta_full;   // [kMetaSlots]
     uint64_t* meta_empty;  // [kMetaSlots]  the 8 correction warps have read the slot
-    uint64_t* s_full;      // [2]  both: QK_g done
-    uint64_t* p_full;      // [2]  even CTA: P_g (and the mass pieces) of all 256 rows in TMEM
-    uint64_t* o_full;      // [2]  both: PV_g done; also frees K/V stage g % kStages
-    uint64_t* o_free;      // [2]  even CTA: both corrections have read O_g
+    uint64_t* s_full;      // [1]  both: QK_g done
+    uint64_t* s_free;      // [1]  even CTA: the softmax of all 256 rows has read S_g
+    uint64_t* p_full;      // [2]  even CTA: P_g of all 256 rows in P_b, b = g % 2
+    uint64_t* o_full;      // [2]  both: PV_g done, for the tiles g of parity b
+    uint64_t* o_free;      // [2]  even CTA: both corrections have read O for a tile of parity b
     uint64_t* st_full;     // [kStatSlots]  alpha / mass of tile g
     uint64_t* st_free;     // [kStatSlots]
     uint64_t* drain;       // [2]  one per MMA thread
@@ -146,6 +157,7 @@ __device__ __forceinline__ Bars bars_at(uint8_t* smem) {
     r.meta_full = b; b += kMetaSlots;
     r.meta_empty = b; b += kMetaSlots;
     r.s_full = b; b += 2;
+    r.s_free = b; b += 2;
     r.p_full = b; b += 2;
     r.o_full = b; b += 2;
     r.o_free = b; b += 2;
@@ -299,27 +311,23 @@ __device__ __forceinline__ uint32_t cvt_relu_f16x2(float hi, float lo) {
     asm("cvt.rn.relu.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
     return d;
 }
-__device__ __forceinline__ uint32_t cvt_bf16x2(float hi, float lo) {
-    uint32_t d;
-    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
-    return d;
-}
 
 // The items of cluster `c` are c, c + ncl, ...
 __device__ __forceinline__ int local_items(int items, int c, int ncl) {
     return c < items ? (items - c + ncl - 1) / ncl : 0;
 }
 
-template <bool HAS_MEAN>
+template <bool EXPCAST>
 __device__ void producer(const Params& p, uint8_t* smem, const Bars& B, const Waiter& wait, uint32_t rank, int c,
                          int ncl) {
+    const CUtensorMap* tm_v = rank ? &p.tm_v1 : &p.tm_v0;
+    const int v_row0 = rank ? (EXPCAST ? kVRows0 : 64) : 0;   // first V channel this CTA loads
     prefetch_tmap(&p.tm_q);
     prefetch_tmap(&p.tm_k);
-    prefetch_tmap(&p.tm_v);
-    if (HAS_MEAN) prefetch_tmap(&p.tm_mop);
+    prefetch_tmap(tm_v);
     const uint32_t lead_q = peer_addr(B.q_full, 0);       // q_full[b] at + 8 b
     const uint32_t lead_kv = peer_addr(B.kv_full, 0);     // kv_full[s] at + 8 s
-    const uint32_t kv_bytes = 2 * (2 * kHalf + (HAS_MEAN ? kMopHalf : 0));
+    const uint32_t kv_bytes = 2 * kHalf + 128 * 128;      // both K halves, all 128 V channel rows
     uint32_t g = 0, li = 0;
     int q_loaded = 0;          // items whose Q this CTA has requested
     uint32_t loaded = 0;       // tiles requested
@@ -340,10 +348,8 @@ __device__ void producer(const Params& p, uint8_t* smem, const Bars& B, const Wa
             }
             uint8_t* st = smem + kOffStages + s * kStageBytes;
             if (rank == 0) mbar_arrive_expect_tx(&B.kv_full[s], kv_bytes);
-            const int row = j * kBN + 64 * (int)rank;
-            tma_load_3d_pair(st, &p.tm_k, lead_kv + 8 * s, 0, row, head);
-            tma_load_3d_pair(st + kHalf, &p.tm_v, lead_kv + 8 * s, 0, row, head);
-            if (HAS_MEAN) tma_load_3d_pair(st + 2 * kHalf, &p.tm_mop, lead_kv + 8 * s, 0, row, head);
+            tma_load_3d_pair(st, &p.tm_k, lead_kv + 8 * s, 0, j * kBN + 64 * (int)rank, head);
+            tma_load_3d_pair(st + kHalf, tm_v, lead_kv + 8 * s, 0, j * 128 + v_row0, head);
             loaded = g + 1;
         }
     }
@@ -363,9 +369,12 @@ __device__ void producer(const Params& p, uint8_t* smem, const Bars& B, const Wa
     }
 }
 
-// The per-tile V scales (512 B) run on their own deeper ring, so a K/V stage
-// is free as soon as the PV of its tile has been committed.
+// The per-tile V scales (and with V-Smooth the stored means u = mu / vscale,
+// core.py:114) run on their own deeper ring, so a K/V stage is free as soon
+// as the PV of its tile has been committed.
+template <bool HAS_MEAN>
 __device__ void meta_producer(const Params& p, uint8_t* smem, const Bars& B, const Waiter& wait, int c, int ncl) {
+    constexpr uint32_t bytes = HAS_MEAN ? 1024 : 512;
     uint32_t g = 0, loaded = 0;
     bool ok = true;
     for (int it = c; ok && it < p.items; it += ncl) {
@@ -377,8 +386,8 @@ __device__ void meta_producer(const Params& p, uint8_t* smem, const Bars& B, con
                 ok = false;
                 break;
             }
-            mbar_arrive_expect_tx(&B.meta_full[s], kMetaBytes);
-            bulk_load(smem + kOffMeta + s * kMetaBytes, meta + (int64_t)j * 256, kMetaBytes, &B.meta_full[s]);
+            mbar_arrive_expect_tx(&B.meta_full[s], bytes);
+            bulk_load(smem + kOffMeta + s * kMetaBytes, meta + (int64_t)j * 256, bytes, &B.meta_full[s]);
             loaded = g + 1;
         }
     }
@@ -413,115 +422,93 @@ __device__ __forceinline__ void mma2_ts(uint32_t d_tmem, uint32_t a_tmem, uint32
         ::"r"(d_tmem), "r"(a_tmem), "r"(b_lo), "r"(hi), "r"(idesc), "r"(accumulate)
         : "memory");
 }
-// D += A B^T with bf16 A in tensor memory and bf16 B in shared memory (K = 16)
-__device__ __forceinline__ void mma2_ts_bf16(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t hi,
-                                             uint32_t idesc) {
-    asm volatile(
-        "{\n\t.reg .b64 db;\n\t"
-        "mov.b64 db, {%2, %3};\n\t"
-        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], db, %4, 1;\n\t}"
-        ::"r"(d_tmem), "r"(a_tmem), "r"(b_lo), "r"(hi), "r"(idesc)
-        : "memory");
-}
-
-// Instruction descriptor, kind::f16 with bf16 A and B (format 1 at [7,10)
-// and [10,13)), F32 D, both K-major.
-__host__ __device__ constexpr uint32_t idesc_bf16_f32(int m, int n) {
-    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
-}
-
-// Shared-memory descriptor for a K-major operand laid out by a TMA load with
-// 32-byte swizzle: rows of 32 bytes, 8-row atoms 256 bytes apart (SBO),
-// layout type 6 = SWIZZLE_32B at [61,64), version 1 at [46,48).
-__device__ __forceinline__ uint64_t smem_desc_k32(const void* p) {
-    const uint64_t addr = smem_u32(p);
-    return ((addr & 0x3FFFFull) >> 4) | (1ull << 16) | ((256ull >> 4) << 32) | (1ull << 46) | (6ull << 61);
-}
-
 // Two MMA threads of the even CTA, on different SM sub-partitions, split the
-// issue work: thread X (warp 1 for X = 0, warp 3 for X = 1) owns TMEM buffers
-// S_X / O_X and issues PV_g then QK_{g+2} for the tiles g of its parity, g
-// running over the tiles of all items of this pair.  No accumulator is shared
-// between the threads, so the tensor pipe may interleave their MMAs freely;
-// each thread's own issue order keeps QK_{g+2} after the PV_g that reads P_g
-// from the same buffer.  Every MMA instruction waits for issue slots next to
-// the busy softmax and correction warps, so two issuers halve the per-tile
-// issue latency on the critical path.  The loop is unrolled by the thread's
-// two K/V stages (X and X + 2), so stage and buffer offsets are constants.
-template <bool HAS_MEAN, uint32_t X>
-__device__ void mma_issuer(const Params& p, uint8_t* smem, const Bars& B, const Waiter& wait, uint32_t tmem, int c,
-                           int ncl) {
-    static_assert(kStages == 8, "two issuers with four stages each");
+// issue work: warp 1 issues every QK, warp 3 every PV, g running over the
+// tiles of all items of this pair.  They share no tensor memory (QK writes S;
+// PV reads P_b and writes O_b), so the tensor pipe may interleave their MMAs
+// freely.  Every MMA instruction waits for issue slots next to the busy
+// softmax and correction warps, so each thread's stream is kept short.
+
+// S_g = Q8 K8_g^T into the one S buffer, as soon as K_g has landed and the
+// softmax has read S_{g-1} into registers.  The q_free commit after an item's
+// last QK frees its Q buffer once those MMAs complete.
+__device__ void qk_issuer(const Params& p, uint8_t* smem, const Bars& B, const Waiter& wait, uint32_t tmem, int c,
+                          int ncl) {
     const uint32_t idesc = idesc_e4m3_f32(2 * kBM, kBN);
-    const uint32_t idesc_mean = idesc_bf16_f32(2 * kBM, kBN);
     const uint64_t q64 = smem_desc_k128(smem + kOffQ);
     const uint32_t hi = (uint32_t)(q64 >> 32);
     const uint32_t q0lo = (uint32_t)q64;
     const uint32_t k0lo = (uint32_t)smem_desc_k128(smem + kOffStages);
-    const uint64_t m64 = smem_desc_k32(smem + kOffStages + 2 * kHalf);
-    const uint32_t mhi = (uint32_t)(m64 >> 32), m0lo = (uint32_t)m64;
-    constexpr uint32_t kStageLo = kStageBytes >> 4, kHalfLo = kHalf >> 4, kQLo = kQBytes >> 4;
+    constexpr uint32_t kStageLo = kStageBytes >> 4, kQLo = kQBytes >> 4;
     const uint32_t T = (uint32_t)p.T;
-    const uint32_t G = (uint32_t)local_items(p.items, c, ncl) * T;
-    const uint32_t d = tmem + kColS + X * kBN, od = tmem + kColO + X * 128;
-    // cursor of this thread's next QK: local item and tile; every item the
-    // cursor leaves gets this thread's q_free arrival (count 2: both threads)
-    uint32_t qli = 0, qj = X, q_waited = 0xffffffffu;
-    while (qj >= T) {                   // an item of one tile holds no QK of thread 1
-        qj -= T;
-        commit_both(&B.q_free[qli & 1]);
-        ++qli;
-    }
-    auto qk = [&](uint32_t s2) -> bool {
-        if (qli != q_waited) {
-            if (!wait(&B.q_full[qli & 1], (qli >> 1) & 1)) return false;
+    const int nitems = local_items(p.items, c, ncl);
+    const uint32_t d = tmem + kColS;
+    uint32_t g = 0;
+    bool ok = true;
+    for (int li = 0; ok && li < nitems; ++li) {
+        if (!wait(&B.q_full[li & 1], (li >> 1) & 1)) break;
+        const uint32_t qlo = q0lo + (li & 1) * kQLo;
+        for (uint32_t j = 0; j < T; ++j, ++g) {
+            const uint32_t s = g % kStages;
+            if (!wait.all(&B.kv_full[s], (g / kStages) & 1, g >= 1 ? &B.s_free[0] : nullptr, (g - 1) & 1)) {
+                ok = false;
+                break;
+            }
             tc_fence_after();
-            q_waited = qli;
-        }
-        const uint32_t qlo = q0lo + (qli & 1) * kQLo, klo = k0lo + s2 * kStageLo;
+            const uint32_t klo = k0lo + s * kStageLo;
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) mma2_ss(d, qlo + 2 * kk, klo + 2 * kk, hi, idesc, kk > 0);
-        commit_both(&B.s_full[X]);
-        qj += 2;
-        while (qj >= T) {               // this thread's QKs of item qli are all issued
-            qj -= T;
-            commit_both(&B.q_free[qli & 1]);
-            ++qli;
+            for (int kk = 0; kk < 4; ++kk) mma2_ss(d, qlo + 2 * kk, klo + 2 * kk, hi, idesc, kk > 0);
+            commit_both(&B.s_full[0]);
         }
+        if (ok) commit_both(&B.q_free[li & 1]);
+    }
+    commit_local_pair(&B.drain[0]);
+    drain_wait(&B.drain[0], 0);
+}
+
+// O_b = P_g [V8_g | 1] with b = g % 2 (ExpCast, N = 144), or P_g V8_g (N =
+// 128) with b = g % 2.  PV_g
+// waits for P_g, for the corrections' read of O_b (tile g - 2) and for its
+// stage.  The commit that signals PV_g done (o_full, to both CTAs) also
+// frees K/V stage g % kStages (QK_g, which read the stage's K, completed
+// before the softmax of tile g began).  The loop is unrolled by the 8
+// stages, so stage and buffer offsets are constants.
+template <bool EXPCAST>
+__device__ void pv_issuer(const Params& p, uint8_t* smem, const Bars& B, const Waiter& wait, uint32_t tmem, int c,
+                          int ncl) {
+    static_assert(kStages == 8, "the unrolled loop");
+    const uint32_t idesc = idesc_e4m3_f32(2 * kBM, EXPCAST ? kPvN : 128);
+    const uint64_t k64 = smem_desc_k128(smem + kOffStages);
+    const uint32_t hi = (uint32_t)(k64 >> 32);
+    const uint32_t v0lo = (uint32_t)k64 + (kHalf >> 4);
+    constexpr uint32_t kStageLo = kStageBytes >> 4;
+    const uint32_t G = (uint32_t)local_items(p.items, c, ncl) * (uint32_t)p.T;
+    auto step = [&](auto S_, uint32_t g) -> bool {
+        constexpr uint32_t s = decltype(S_)::value, b = s & 1;   // g % kStages, g % 2
+        if (!wait.all(&B.p_full[b], (g >> 1) & 1, g >= 2 ? &B.o_free[b] : nullptr, ((g - 2) >> 1) & 1,
+                      &B.kv_full[s], (g / kStages) & 1))
+            return false;
+        tc_fence_after();
+        const uint32_t pa = tmem + (b ? kColP1 : kColP0), od = tmem + (b ? kColO1 : kColO0);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) mma2_ts(od, pa + 8 * kk, v0lo + s * kStageLo + 2 * kk, hi, idesc, kk > 0);
+        commit_both(&B.o_full[b]);
+        commit_both(&B.kv_empty[s]);     // the producers may refill stage s
         return true;
     };
     bool ok = true;
-    if (X < G) {
-        ok = wait(&B.kv_full[X], 0);
-        if (ok) {
-            tc_fence_after();
-            ok = qk(X);
-        }
+    for (uint32_t g = 0; ok && g < G; g += 8) {
+        ok = step(std::integral_constant<uint32_t, 0>{}, g);
+        if (ok && g + 1 < G) ok = step(std::integral_constant<uint32_t, 1>{}, g + 1);
+        if (ok && g + 2 < G) ok = step(std::integral_constant<uint32_t, 2>{}, g + 2);
+        if (ok && g + 3 < G) ok = step(std::integral_constant<uint32_t, 3>{}, g + 3);
+        if (ok && g + 4 < G) ok = step(std::integral_constant<uint32_t, 4>{}, g + 4);
+        if (ok && g + 5 < G) ok = step(std::integral_constant<uint32_t, 5>{}, g + 5);
+        if (ok && g + 6 < G) ok = step(std::integral_constant<uint32_t, 6>{}, g + 6);
+        if (ok && g + 7 < G) ok = step(std::integral_constant<uint32_t, 7>{}, g + 7);
     }
-    auto step = [&](auto S_, uint32_t g) -> bool {
-        constexpr uint32_t s = decltype(S_)::value, s2 = (s + 2) % kStages;   // g % kStages
-        const bool next = g + 2 < G;
-        if (!wait.all(&B.p_full[X], (g >> 1) & 1, g >= 2 ? &B.o_free[X] : nullptr, ((g - 2) >> 1) & 1,
-                      next ? &B.kv_full[s2] : nullptr, ((g + 2) / kStages) & 1))
-            return false;
-        tc_fence_after();
-        const uint32_t vlo = k0lo + s * kStageLo + kHalfLo;
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) mma2_ts(od, d + (kk >> 1) * 64 + (kk & 1) * 8, vlo + 2 * kk, hi, idesc, kk > 0);
-        if (HAS_MEAN) mma2_ts_bf16(od, d + kColMass, m0lo + s * kStageLo, mhi, idesc_mean);
-        commit_both(&B.o_full[X]);
-        commit_both(&B.kv_empty[s]);     // the producers may refill stage s
-        if (next) return qk(s2);
-        return true;
-    };
-    for (uint32_t g = X; ok && g < G; g += 8) {
-        ok = step(std::integral_constant<uint32_t, X>{}, g);
-        if (ok && g + 2 < G) ok = step(std::integral_constant<uint32_t, X + 2>{}, g + 2);
-        if (ok && g + 4 < G) ok = step(std::integral_constant<uint32_t, X + 4>{}, g + 4);
-        if (ok && g + 6 < G) ok = step(std::integral_constant<uint32_t, X + 6>{}, g + 6);
-    }
-    commit_local_pair(&B.drain[X]);
-    drain_wait(&B.drain[X], 0);
+    commit_local_pair(&B.drain[1]);
+    drain_wait(&B.drain[1], 0);
 }
 
 // Two threads of one warp per query row: warp w (quarter w % 4, sub (w-4)/4)
@@ -548,24 +535,17 @@ __device__ __forceinline__ void tmem_ld16x2_at(uint32_t taddr, uint32_t (&r)[N])
           "=r"(r[OFF + 30]), "=r"(r[OFF + 31])
         : "r"(taddr));
 }
+// thread t < 16: lane base + t, columns [c, c + 16); thread t + 16: the same
+// lane, columns [c + 16, c + 32): one row's 128 codes in 32 columns
 __device__ __forceinline__ void tmem_st16x2_16(uint32_t taddr, const uint32_t (&r)[16]) {
     asm volatile(
-        "tcgen05.st.sync.aligned.16x32bx2.x16.b32 [%0], 64, {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
+        "tcgen05.st.sync.aligned.16x32bx2.x16.b32 [%0], 16, {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
         "%13, %14, %15, %16};"
         ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
           "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
         : "memory");
 }
-// thread t < 16: lane base + t, columns [c, c + 4); thread t + 16: the same
-// lane, columns [c + 4, c + 8): one row's 8 consecutive columns from the pair
-__device__ __forceinline__ void tmem_st16x2_4_split4(uint32_t taddr, uint32_t a, uint32_t b, uint32_t c,
-                                                     uint32_t d) {
-    asm volatile("tcgen05.st.sync.aligned.16x32bx2.x4.b32 [%0], 4, {%1, %2, %3, %4};"
-                 ::"r"(taddr), "r"(a), "r"(b), "r"(c), "r"(d)
-                 : "memory");
-}
-
-template <bool EXPCAST, bool HAS_MEAN, bool PROBE>
+template <bool EXPCAST, bool PROBE>
 __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, const Waiter& wait, uint32_t tmem,
                              uint32_t rank, int c, int ncl, int quarter, int sub, int lane) {
     // warp (quarter, sub) owns rows quarter*32 + sub*16 + [0, 16); lanes t and
@@ -575,6 +555,7 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, cons
     float* st_alpha = reinterpret_cast<float*>(smem + kOffStats);
     float* st_mass = st_alpha + kStatSlots * 128;               // [kStatSlots][128]
     const uint32_t lead_p = peer_addr(B.p_full, 0);            // p_full[b] at + 8 b
+    const uint32_t lead_s = peer_addr(B.s_free, 0);
     const uint32_t trow = tmem + ((uint32_t)(quarter * 32 + sub * 16) << 16);
     const int kstep = p.kq / kBN;
     uint32_t g = 0;
@@ -596,18 +577,24 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, cons
                 kcnt = 0;
                 ++kidx;
             }
-            const uint32_t ts = trow + kColS + b * kBN;
+            const uint32_t ts = trow + kColS;
             const int slot = g % kStatSlots;
             // the scores of tile g, and (checked alongside) the statistics
-            // slot this tile writes at its end
-            if (!wait.all(&B.s_full[b], (g >> 1) & 1,
-                          g >= (uint32_t)kStatSlots ? &B.st_free[slot] : nullptr, ((g / kStatSlots) - 1) & 1))
+            // slot this tile writes at its end and the completion of PV_{g-2},
+            // the last reader of the P buffer this tile writes
+            if (!wait.all(&B.s_full[0], g & 1,
+                          g >= (uint32_t)kStatSlots ? &B.st_free[slot] : nullptr, ((g / kStatSlots) - 1) & 1,
+                          g >= 2 ? &B.o_full[b] : nullptr, ((g - 2) >> 1) & 1))
                 return;
             tc_fence_after();
             uint32_t r[64];
             tmem_ld16x2_at<0>(ts, r);
             tmem_ld16x2_at<32>(ts + 32, r);
             tmem_wait_ld();
+            // S is in registers: QK_{g+1} may overwrite it
+            tc_fence_before();
+            __syncwarp();
+            mbar_arrive_cluster_if(lead_s, lane == 0);
             if (j == p.T - 1) {             // only the last tile of an item can be partial
                 const int nvalid = (int)(p.sk - (int64_t)j * kBN) - 64 * hs;
                 if (nvalid < 64) {
@@ -650,7 +637,7 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, cons
                 Bc = __fsub_rn(8.0f, __fmul_rn(m_new, kLog2e));
             }
             const float2 AA = make_float2(A, A), BB = make_float2(Bc, Bc);
-            float ms[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            float ms[4] = {0.0f, 0.0f, 0.0f, 0.0f};   // exp: the FP32 row mass of sum(p * 256)
             uint32_t pk[16];
 #pragma unroll
             for (int w = 0; w < 16; ++w) {
@@ -662,9 +649,6 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, cons
                     const uint32_t h01 = cvt_relu_f16x2(g01.y, g01.x);   // integer codes as f16 subnormals
                     const uint32_t h23 = cvt_relu_f16x2(g23.y, g23.x);
                     pk[w] = __byte_perm(h01, h23, 0x6420);
-                    // code << 7 read as f16 is exactly decode(code) / 256
-                    add_f16x2_to_f32(ms[0], ms[1], h01 << 7);
-                    add_f16x2_to_f32(ms[2], ms[3], h23 << 7);
                 } else {
                     const float e0 = ex2_ftz(g01.x), e1 = ex2_ftz(g01.y), e2 = ex2_ftz(g23.x), e3 = ex2_ftz(g23.y);
                     // packed adds: each lane is the same round-to-nearest FP32 add
@@ -674,11 +658,14 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, cons
                     pk[w] = e4m3x2(e0, e1) | (e4m3x2(e2, e3) << 16);
                 }
             }
-            // ExpCast: ms holds sum(p) = mass; scale to units of 256.  Otherwise
-            // ms already holds sum(p * 256).  The row's two halves add up to M.
-            float Mh = __fadd_rn(__fadd_rn(ms[0], ms[1]), __fadd_rn(ms[2], ms[3]));
-            if (EXPCAST) Mh = __fmul_rn(Mh, 256.0f);
-            const float M = __fadd_rn(Mh, __shfl_xor_sync(0xffffffffu, Mh, 16));
+            // ExpCast's row mass is the sum of the decoded P, which the PV MMA
+            // forms in its ones columns.  The exp mode keeps the FP32 sum of the
+            // unrounded p * 256; the row's two halves add up to M.
+            float M = 0.0f;
+            if (!EXPCAST) {
+                const float Mh = __fadd_rn(__fadd_rn(ms[0], ms[1]), __fadd_rn(ms[2], ms[3]));
+                M = __fadd_rn(Mh, __shfl_xor_sync(0xffffffffu, Mh, 16));
+            }
             if (probe && j >= p.pr_begin && j < p.pr_begin + p.pr_count) {
                 const int64_t t = j - p.pr_begin;
                 float* lg = p.pr_logits + (t * 128 + row) * 128 + hs * 64;
@@ -692,24 +679,12 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, cons
                     rs[0] = m_new; rs[1] = A; rs[2] = Bc; rs[3] = alpha;
                 }
             }
-            // P_g over this thread's own (already read) S_g columns: 4 codes per
-            // 32-bit column, the A-operand layout of the PV MMA
-            tmem_st16x2_16(ts, pk);
-            if (HAS_MEAN) {
-                // the row mass as bf16 pieces M1 + M2 + M3 (each remainder exact
-                // in FP32), in the K slots [M1, M1, M1, M2, M2, M3, 0 ...] that
-                // meet [u1, u2, u3, u1, u2, u1, 0 ...] of the mean operand
-                const uint32_t p1 = cvt_bf16x2(M, M);
-                const float r1 = __fsub_rn(M, __uint_as_float(p1 << 16));
-                const uint32_t p2 = cvt_bf16x2(r1, r1);
-                const float r2 = __fsub_rn(r1, __uint_as_float(p2 << 16));
-                const uint32_t w1 = __byte_perm(p1, p2, 0x5410);   // (M1, M2)
-                const uint32_t w2 = cvt_bf16x2(r2, r1);              // (M2, M3)
-                tmem_st16x2_4_split4(ts + kColMass, hs ? 0u : p1, hs ? 0u : w1, hs ? 0u : w2, 0u);
-            }
+            // P_g into P_b: 4 codes per 32-bit column, the A-operand layout of
+            // the PV MMA (K slice kk of 32 keys in columns [8 kk, 8 kk + 8))
+            tmem_st16x2_16(trow + (b ? kColP1 : kColP0), pk);
             if (hs == 0) {
                 st_alpha[slot * 128 + row] = alpha;
-                st_mass[slot * 128 + row] = M;
+                if (!EXPCAST) st_mass[slot * 128 + row] = M;
             }
             tmem_wait_st();
             tc_fence_before();
@@ -721,6 +696,21 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, cons
     }
 }
 
+// One TMEM column of the warp's 32 lanes: thread i gets lane i.
+__device__ __forceinline__ uint32_t tmem_ld32_x1(uint32_t taddr) {
+    uint32_t r;
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr));
+    return r;
+}
+
+// Two threads per row (warp (quarter, half): rows quarter * 32 + lane,
+// channels half * 64 + [0, 64)).  Per tile, in units of 256 as the softmax:
+// acc = alpha acc + (PV + M mu / vscale) vscale (core.py:335-336: rowmass
+// times the stored scaled mean, then the scale), den = alpha den + M.
+// ExpCast reads M from the mass column of O_b; the exp mode from the
+// softmax's statistics ring.  O_b is released (o_free) once both chunks of
+// it are in registers.
+template <bool EXPCAST, bool HAS_MEAN>
 __device__ void correction_role(const Params& p, uint8_t* smem, const Bars& B, const Waiter& wait, uint32_t tmem,
                                 uint32_t rank, int c, int ncl, int quarter, int half, int lane) {
     const int row = quarter * 32 + lane;
@@ -744,13 +734,14 @@ __device__ void correction_role(const Params& p, uint8_t* smem, const Bars& B, c
                 return;
             tc_fence_after();
             const float alpha = st_alpha[slot * 128 + row];
-            const float M = st_mass[slot * 128 + row];
+            float M = EXPCAST ? 0.0f : st_mass[slot * 128 + row];
             __syncwarp();
             mbar_arrive_if(&B.st_free[slot], lane == 0);
             const float4* vsp = reinterpret_cast<const float4*>(smem + kOffMeta + s * kMetaBytes);
+            const float4* usp = vsp + 32;                          // the stored means follow the scales
             const bool rescale = __any_sync(0xffffffffu, alpha != 1.0f);
             const float2 aa = make_float2(alpha, alpha);
-            const uint32_t to = trow + kColO + b * 128 + c0;
+            const uint32_t ob = trow + (b ? kColO1 : kColO0);
             if (rescale) {      // warp-uniform; alpha == 1 leaves acc unchanged
 #pragma unroll
                 for (int i = 0; i < 32; ++i) acc[i] = fmul2(acc[i], aa);
@@ -758,21 +749,30 @@ __device__ void correction_role(const Params& p, uint8_t* smem, const Bars& B, c
 #pragma unroll
             for (int ch = 0; ch < 2; ++ch) {
                 uint32_t o[32];
-                tmem_ld32_at<0>(to + 32 * ch, o);
+                tmem_ld32_at<0>(ob + c0 + 32 * ch, o);
+                uint32_t mraw = 0;
+                if (EXPCAST && ch == 0) mraw = tmem_ld32_x1(ob + kColMass);
                 tmem_wait_ld();
+                if (EXPCAST && ch == 0) M = __uint_as_float(mraw);
                 if (ch == 1) {
                     tc_fence_before();
                     __syncwarp();
                     mbar_arrive_cluster_if(lead_o + 8 * b, lane == 0);
                 }
+                const float2 mm = make_float2(M, M);
 #pragma unroll
                 for (int q = 0; q < 8; ++q) {
                     const float4 vs = vsp[(c0 >> 2) + 8 * ch + q];
                     const int i = 16 * ch + 2 * q;
-                    acc[i] = ffma2(make_float2(__uint_as_float(o[4 * q]), __uint_as_float(o[4 * q + 1])),
-                                   make_float2(vs.x, vs.y), acc[i]);
-                    acc[i + 1] = ffma2(make_float2(__uint_as_float(o[4 * q + 2]), __uint_as_float(o[4 * q + 3])),
-                                       make_float2(vs.z, vs.w), acc[i + 1]);
+                    float2 o01 = make_float2(__uint_as_float(o[4 * q]), __uint_as_float(o[4 * q + 1]));
+                    float2 o23 = make_float2(__uint_as_float(o[4 * q + 2]), __uint_as_float(o[4 * q + 3]));
+                    if (HAS_MEAN) {
+                        const float4 u = usp[(c0 >> 2) + 8 * ch + q];
+                        o01 = ffma2(mm, make_float2(u.x, u.y), o01);
+                        o23 = ffma2(mm, make_float2(u.z, u.w), o23);
+                    }
+                    acc[i] = ffma2(o01, make_float2(vs.x, vs.y), acc[i]);
+                    acc[i + 1] = ffma2(o23, make_float2(vs.z, vs.w), acc[i + 1]);
                 }
             }
             den = __fadd_rn(__fmul_rn(alpha, den), M);
@@ -829,9 +829,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
     if (threadIdx.x == 0) {
         for (int i = 0; i < 2; ++i) {
             mbar_init(&B.q_full[i], 1);
-            mbar_init(&B.q_free[i], 2);           // both MMA threads
+            mbar_init(&B.q_free[i], 1);           // the QK thread
             mbar_init(&B.drain[i], 1);
             mbar_init(&B.s_full[i], 1);
+            mbar_init(&B.s_free[i], 16);          // 8 softmax warps in each CTA
             mbar_init(&B.p_full[i], 16);          // 8 softmax warps in each CTA
             mbar_init(&B.o_full[i], 1);
             mbar_init(&B.o_free[i], 16);          // 8 correction warps in each CTA
@@ -851,6 +852,19 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
         *abort = 0;
         fence_barrier_init();
     }
+    if (EXPCAST && rank == 1) {
+        // the odd CTA's constant B rows 56..71 of every stage: E4M3 1.0 (0x38)
+        // in every byte, so the 128-byte swizzle needs no care; written before
+        // the cluster barrier, and made visible to the tensor cores' (async)
+        // proxy by each writing thread
+        constexpr uint32_t kOnesBytes = (uint32_t)(kVRows0 - kVRows1) * 128;   // 2 KB per stage
+        for (uint32_t i = threadIdx.x; i < kStages * (kOnesBytes / 16); i += kThreads) {
+            const uint32_t st = i / (kOnesBytes / 16), off = i % (kOnesBytes / 16);
+            reinterpret_cast<uint4*>(smem + kOffStages + st * kStageBytes + kHalf + kVRows1 * 128)[off] =
+                make_uint4(0x38383838u, 0x38383838u, 0x38383838u, 0x38383838u);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
     if (warp == 1) {
         tmem_alloc_pair(tmem_slot, kTmemCols);
         tmem_relinquish_pair();
@@ -867,16 +881,16 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
     // correction groups 112; 10240 + 22528 + 28672 = 61440.
     if (warp < 4) {
         reg_dealloc<80>();
-        if (warp == 0 && lane == 0) producer<HAS_MEAN>(p, smem, B, wait, rank, c, ncl);
-        if (warp == 1 && lane == 0 && rank == 0) mma_issuer<HAS_MEAN, 0>(p, smem, B, wait, tmem, c, ncl);
-        if (warp == 3 && lane == 0 && rank == 0) mma_issuer<HAS_MEAN, 1>(p, smem, B, wait, tmem, c, ncl);
-        if (warp == 2 && lane == 0) meta_producer(p, smem, B, wait, c, ncl);
+        if (warp == 0 && lane == 0) producer<EXPCAST>(p, smem, B, wait, rank, c, ncl);
+        if (warp == 1 && lane == 0 && rank == 0) qk_issuer(p, smem, B, wait, tmem, c, ncl);
+        if (warp == 3 && lane == 0 && rank == 0) pv_issuer<EXPCAST>(p, smem, B, wait, tmem, c, ncl);
+        if (warp == 2 && lane == 0) meta_producer<HAS_MEAN>(p, smem, B, wait, c, ncl);
     } else if (warp < 12) {
         reg_dealloc<88>();
-        softmax_role<EXPCAST, HAS_MEAN, PROBE>(p, smem, B, wait, tmem, rank, c, ncl, warp & 3, (warp - 4) >> 2, lane);
+        softmax_role<EXPCAST, PROBE>(p, smem, B, wait, tmem, rank, c, ncl, warp & 3, (warp - 4) >> 2, lane);
     } else {
         reg_alloc<112>();
-        correction_role(p, smem, B, wait, tmem, rank, c, ncl, warp & 3, (warp - 12) >> 2, lane);
+        correction_role<EXPCAST, HAS_MEAN>(p, smem, B, wait, tmem, rank, c, ncl, warp & 3, (warp - 12) >> 2, lane);
     }
     tc_fence_before();
     __syncwarp();
@@ -1021,10 +1035,6 @@ __global__ void __launch_bounds__(128, 1)
 }  // namespace
 
 int attn_run(const vcb_attn_args* a, const vcb_attn_probe* probe, cudaStream_t st) {
-    if (a->has_mean && !a->v_mean_op)
-        return fail(VCB_ERR_INVALID_ARGUMENT, "has_mean needs the mean operand (v_mean_op) of vcb_prepare_v");
-    if (a->has_mean && (reinterpret_cast<uintptr_t>(a->v_mean_op) & 15u))
-        return fail(VCB_ERR_INVALID_ARGUMENT, "v_mean_op must be 16-byte aligned");
     Params p;
     memset(&p, 0, sizeof(p));
     const int64_t sq_pad = vcb_padded_rows(a->sq, a->q_block);
@@ -1039,8 +1049,9 @@ int attn_run(const vcb_attn_args* a, const vcb_attn_probe* probe, cudaStream_t s
         return fail(VCB_ERR_INVALID_ARGUMENT, "problem too large for the attention kernel's tile counters");
     int rc = make_map(&p.tm_q, a->q8, 128, (uint64_t)sq_pad, (uint64_t)a->heads, kBM);
     if (!rc) rc = make_map(&p.tm_k, a->k8, 128, (uint64_t)sk_pad, (uint64_t)a->heads, 64);
-    if (!rc) rc = make_map(&p.tm_v, a->v8, 128, (uint64_t)T * 128, (uint64_t)a->heads, 64);
-    if (!rc && a->has_mean) rc = make_map(&p.tm_mop, a->v_mean_op, 32, (uint64_t)T * 128, (uint64_t)a->heads, 64);
+    const uint32_t v_rows0 = a->expcast ? kVRows0 : 64, v_rows1 = a->expcast ? kVRows1 : 64;
+    if (!rc) rc = make_map(&p.tm_v0, a->v8, 128, (uint64_t)T * 128, (uint64_t)a->heads, v_rows0);
+    if (!rc) rc = make_map(&p.tm_v1, a->v8, 128, (uint64_t)T * 128, (uint64_t)a->heads, v_rows1);
     if (rc) return rc;
     p.q_scale = a->q_scale;
     p.k_scale = a->k_scale;

@@ -297,13 +297,6 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
     return d;
 }
 
-// acc (fp32) += the two f16 halves of h, one mixed-precision add each (sm_100).
-__device__ __forceinline__ void add_f16x2_to_f32(float& acc0, float& acc1, uint32_t h) {
-    asm("{\n\t.reg .f16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
-        "add.rn.f32.f16 %0, lo, %0;\n\tadd.rn.f32.f16 %1, hi, %1;\n\t}"
-        : "+f"(acc0), "+f"(acc1) : "r"(h));
-}
-
 template <uint32_t N> __device__ __forceinline__ void reg_alloc() {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
 }

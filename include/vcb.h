@@ -146,9 +146,8 @@ typedef struct {
     float* v_meta;          /* [heads, T, 2, 128]: vscale, then mu/vscale at mean_type */
     uint16_t* v_mean_op;    /* [heads, T, 128, 16] bf16, written when active (nullable): per channel the
                                stored mean mu/vscale as bf16 pieces u1 + u2 + u3 (u1 truncated, u2 and u3
-                               rounded remainders) in the row [u1, u2, u3, u1, u2, u1, 0 x 10]: a bf16
-                               MMA operand for a caller that folds the mean into its own PV GEMM;
-                               vcb_attention_fp8 does not read it (it takes mu/vscale from v_meta) */
+                               rounded remainders) in the row [u1, u2, u3, u1, u2, u1, 0 x 10], the B
+                               operand of the exp-mode attention kernel's row-mass x mean MMA */
     int32_t* status;        /* device status word (nullable) */
 } vcb_v_args;
 
@@ -161,7 +160,8 @@ typedef struct {
     const uint8_t* q8; const float* q_scale;
     const uint8_t* k8; const float* k_scale;
     const uint8_t* v8; const float* v_meta;
-    const uint16_t* v_mean_op;  /* not read (nullable); the mean comes from v_meta */
+    const uint16_t* v_mean_op;  /* vcb_v_args.v_mean_op; required when has_mean and not expcast (the
+                                   ExpCast kernel takes mu / vscale from v_meta) */
     int64_t heads, sq, sk;
     int dv;
     int q_block, k_quant_block, kv_block;

@@ -57,36 +57,30 @@
 // den256 = 256 den); 256 is a power of two, so no rounding changes.  Every
 // mbarrier wait is bounded (vcb_common.cuh); a CTA that gives up tells its
 // peer, and the pair drains and frees its tensor memory together.
-#include "vcb_internal.h"
+#include "vcb_attn_pair.cuh"
 #include <type_traits>
 
 namespace vcb {
 
 namespace {
 
-constexpr int kBM = 128;                          // query rows per CTA (256 per pair)
-constexpr int kBN = 128;                          // keys per KV tile
 constexpr int kStages = 8;
 constexpr int kMetaSlots = 16;                    // per-tile vscale ring
 constexpr int kThreads = 640;                     // 20 warps: 4 producer/MMA, 8 softmax, 8 correction
-constexpr uint32_t kQBytes = 128 * 128;           // one E4M3 Q tile (16 KB)
-constexpr uint32_t kHalf = 64 * 128;              // this CTA's half of a K tile (8 KB)
-// The PV MMA's B operand.  ExpCast: 72 rows of 128 keys in each CTA (N =
-// 144); the even CTA loads V channels 0..71, the odd CTA channels 72..127
-// into rows 0..55 and keeps E4M3 ones in rows 56..71, so O columns 0..127 are
-// the 128 channels in order and columns 128..143 each hold the row mass
-// sum(P).  The exp mode (its row mass is the FP32 sum of unrounded
-// probabilities, which the softmax forms) loads 64 channels per CTA, N = 128.
-constexpr int kVRows0 = 72, kVRows1 = 56;         // V channels loaded by the even / odd CTA (ExpCast)
+// The PV MMA's B operand: 72 rows of 128 keys in each CTA (N = 144).  The
+// even CTA loads V channels 0..71, the odd CTA channels 72..127 into rows
+// 0..55 and keeps E4M3 ones in rows 56..71, so O columns 0..127 are the 128
+// channels in order and columns 128..143 each hold the row mass sum(P).
+constexpr int kVRows0 = 72, kVRows1 = 56;         // V channels loaded by the even / odd CTA
 constexpr uint32_t kVBytes = 72 * 128;            // one CTA's B rows of a stage (9 KB)
 constexpr uint32_t kStageBytes = kHalf + kVBytes; // 17 KB, a multiple of 1024
 constexpr uint32_t kOffQ = 0;                     // Q buffers 0, 1
 constexpr uint32_t kOffStages = 2 * kQBytes;
 constexpr uint32_t kMetaBytes = 1024;             // vscale[128], stored mean mu / vscale [128]
 constexpr uint32_t kOffMeta = kOffStages + kStages * kStageBytes;
-constexpr int kStatSlots = 8;                     // per-tile alpha / row-mass ring
-constexpr uint32_t kOffStats = kOffMeta + kMetaSlots * kMetaBytes;  // alpha[8][128], mass[8][128]
-constexpr uint32_t kOffBars = kOffStats + 2 * kStatSlots * 128 * 4;
+constexpr int kStatSlots = 8;                     // per-tile alpha ring
+constexpr uint32_t kOffStats = kOffMeta + kMetaSlots * kMetaBytes;  // alpha[8][128]
+constexpr uint32_t kOffBars = kOffStats + kStatSlots * 128 * 4;
 constexpr int kNumBars = 2 + 2 + 2 * kStages + 2 * kMetaSlots + 5 * 2 + 2 * kStatSlots + 2;
 constexpr uint32_t kOffMisc = kOffBars + kNumBars * 8;
 constexpr uint32_t kSmemBytes = kOffMisc + 16;
@@ -102,13 +96,6 @@ constexpr uint32_t kColMass = 128;                // the row-mass column inside 
 constexpr int kPvN = 144;                         // N of the PV MMA with the row-mass columns
 static_assert(kStageBytes % 1024 == 0, "swizzled tiles need 1024-byte aligned stages");
 static_assert(kVRows0 + kVRows1 == 128 && kVRows1 % 8 == 0 && 2 * kVRows0 == kPvN, "V split");
-
-constexpr float kC1 = 11.541560173034668f;        // 8 log2(e) in fp32
-constexpr float kC2 = 119.6500015258789f;         // 119.65 in fp32
-constexpr float kTwoM24 = 5.9604644775390625e-08f;    // 2^-24
-constexpr float kLog2e = 1.4426950408889634f;
-constexpr float kMinNormal = 1.17549435e-38f;     // 2^-126
-constexpr uint32_t kParkHintNs = 20000;           // longest park of a parked wait between checks
 
 struct Params {
     CUtensorMap tm_q, tm_k, tm_v0, tm_v1;      // V boxes of kVRows0 / kVRows1 channel rows
@@ -142,7 +129,7 @@ struct Bars {
     uint64_t* p_full;      // [2]  even CTA: P_g of all 256 rows in P_b, b = g % 2
     uint64_t* o_full;      // [2]  both: PV_g done, for the tiles g of parity b
     uint64_t* o_free;      // [2]  even CTA: both corrections have read O for a tile of parity b
-    uint64_t* st_full;     // [kStatSlots]  alpha / mass of tile g
+    uint64_t* st_full;     // [kStatSlots]  alpha of tile g
     uint64_t* st_free;     // [kStatSlots]
     uint64_t* drain;       // [2]  one per MMA thread
 };
@@ -167,161 +154,10 @@ __device__ __forceinline__ Bars bars_at(uint8_t* smem) {
     return r;
 }
 
-// ------------------------------------------------------------- cluster PTX
-__device__ __forceinline__ uint32_t cluster_rank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-// shared::cluster address of the same shared-memory offset in CTA `rank`
-__device__ __forceinline__ uint32_t peer_addr(const void* p, uint32_t rank) {
-    uint32_t d;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(smem_u32(p)), "r"(rank));
-    return d;
-}
-// Arrive on an mbarrier anywhere in the cluster, with the default
-// (CTA-scope) release.  The data these arrivals publish is tensor memory,
-// ordered for the MMA by tcgen05.wait::st / tcgen05.fence::before_thread_sync
-// before the arrive and tcgen05.fence::after_thread_sync after the wait; a
-// cluster-scope release here cost ~1000 cycles per tile.
-__device__ __forceinline__ void mbar_arrive_cluster_if(uint32_t addr, bool pred) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.u32 p, %1, 0;\n\t"
-        "@p mbarrier.arrive.shared::cluster.b64 _, [%0];\n\t}"
-        ::"r"(addr), "r"((uint32_t)pred)
-        : "memory");
-}
-__device__ __forceinline__ void store_cluster_u32(uint32_t addr, uint32_t v) {
-    asm volatile("st.relaxed.cluster.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
-}
-__device__ __forceinline__ void cluster_sync_all() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-// TMA tile load into this CTA's shared memory whose completion is counted on
-// the even CTA's barrier (`bar` a shared::cluster address); no multicast.
-__device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* map, uint32_t bar, int x, int y,
-                                                 int z) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%3, %4, %5}], [%2];"
-        ::"r"(smem_u32(dst)), "l"(map), "r"(bar), "r"(x), "r"(y), "r"(z)
-        : "memory");
-}
-__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
-    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"
-                 ::"r"(smem_u32(dst_smem)), "r"(ncols) : "memory");
-}
-__device__ __forceinline__ void tmem_relinquish_pair() {
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
-    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
-// Arrives on the barrier at this offset in both CTAs once every tcgen05
-// operation this thread issued before is complete.
-__device__ __forceinline__ void commit_both(uint64_t* bar) {
-    asm volatile(
-        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
-        ::"r"(smem_u32(bar)), "h"((uint16_t)3)
-        : "memory");
-}
-__device__ __forceinline__ void commit_local_pair(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];"
-                 ::"r"(smem_u32(bar)) : "memory");
-}
-
-// Bounded wait used while draining after an abort: ignores the abort flag.
-__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
-    const uint32_t a = smem_u32(bar);
-    const uint64_t t0 = globaltimer();
-    while (!mbar_try_wait_sleep(a, parity, kSuspendHintNs)) {
-        if (globaltimer() - t0 > kWaitLimitNs) return;
-    }
-}
-
-// Non-blocking check of an mbarrier phase.
-__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-
-// A wait that gives up (mbar_wait) and, when it does, raises the peer CTA's
-// abort flag too, so the pair stops together.
-struct Waiter {
-    volatile int* abort;
-    uint32_t peer_abort;     // shared::cluster address of the other CTA's flag
-    __device__ __forceinline__ bool operator()(uint64_t* bar, uint32_t parity) const {
-        if (mbar_wait(bar, parity, abort)) return true;
-        store_cluster_u32(peer_abort, 1u);
-        return false;
-    }
-    // Waits for up to three phases.  A barrier check costs a shared-memory
-    // round trip even when the phase is long complete, so the three checks
-    // are issued back to back (non-blocking test_wait) and their latencies
-    // overlap; only a phase found incomplete falls back to the polling wait.
-    // A null barrier is skipped.
-    __device__ __forceinline__ bool all(uint64_t* b0, uint32_t p0, uint64_t* b1, uint32_t p1, uint64_t* b2 = nullptr,
-                                        uint32_t p2 = 0) const {
-        const bool r0 = mbar_test(smem_u32(b0), p0);
-        const bool r1 = !b1 || mbar_test(smem_u32(b1), p1);
-        const bool r2 = !b2 || mbar_test(smem_u32(b2), p2);
-        if (r0 && r1 && r2) return true;
-        return (r0 || (*this)(b0, p0)) && (r1 || (*this)(b1, p1)) && (r2 || (*this)(b2, p2));
-    }
-    // The same wait parked in the barrier between polls (try_wait with a
-    // suspend-time hint): for roles off the critical path, whose polling would
-    // otherwise take issue slots from the softmax and correction warps that
-    // share their SM sub-partition.
-    __device__ __forceinline__ bool parked(uint64_t* bar, uint32_t parity) const {
-        const uint32_t a = smem_u32(bar);
-        if (mbar_try_wait(a, parity)) return true;
-        const uint64_t t0 = globaltimer();
-        while (!mbar_try_wait_sleep(a, parity, kParkHintNs)) {
-            if (*abort) return false;
-            if (globaltimer() - t0 > kWaitLimitNs) {
-                *abort = 1;
-                store_cluster_u32(peer_abort, 1u);
-                return false;
-            }
-        }
-        return true;
-    }
-};
-
-// 2^x as the single MUFU.EX2 instruction, flushing subnormal results to zero.
-// The softmax's P = 2^g lies in [0, 256]; a result below 2^-126 encodes to
-// E4M3 zero either way and cannot move an FP32 row mass of at least 256, so
-// this gives the same bytes and mass as exp2f with fewer instructions.
-__device__ __forceinline__ float ex2_ftz(float x) {
-    float y;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
-
-__device__ __forceinline__ uint32_t cvt_relu_f16x2(float hi, float lo) {
-    uint32_t d;
-    asm("cvt.rn.relu.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
-    return d;
-}
-
-// The items of cluster `c` are c, c + ncl, ...
-__device__ __forceinline__ int local_items(int items, int c, int ncl) {
-    return c < items ? (items - c + ncl - 1) / ncl : 0;
-}
-
-template <bool EXPCAST>
 __device__ void producer(const Params& p, uint8_t* smem, const Bars& B, const Waiter& wait, uint32_t rank, int c,
                          int ncl) {
     const CUtensorMap* tm_v = rank ? &p.tm_v1 : &p.tm_v0;
-    const int v_row0 = rank ? (EXPCAST ? kVRows0 : 64) : 0;   // first V channel this CTA loads
+    const int v_row0 = rank ? kVRows0 : 0;               // first V channel this CTA loads
     prefetch_tmap(&p.tm_q);
     prefetch_tmap(&p.tm_k);
     prefetch_tmap(tm_v);
@@ -396,32 +232,6 @@ __device__ void meta_producer(const Params& p, uint8_t* smem, const Bars& B, con
             drain_wait(&B.meta_full[s], ((loaded - 1 - s) / kMetaSlots) & 1);
 }
 
-// The MMA thread shares its SM sub-partition with four busy softmax /
-// correction warps, and every instruction it issues waits for a scheduler
-// slot, so its instruction stream is kept short: shared-memory descriptors
-// differ only in the low word (start address >> 4), which the loop advances
-// by constants; the high word (stride, version, swizzle) is one register.
-__device__ __forceinline__ void mma2_ss(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo, uint32_t hi, uint32_t idesc,
-                                        uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t.reg .b64 da, db;\n\t"
-        "mov.b64 da, {%1, %3};\n\t"
-        "mov.b64 db, {%2, %3};\n\t"
-        "setp.ne.b32 p, %5, 0;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], da, db, %4, p;\n\t}"
-        ::"r"(d_tmem), "r"(a_lo), "r"(b_lo), "r"(hi), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-__device__ __forceinline__ void mma2_ts(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t hi, uint32_t idesc,
-                                        uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t.reg .b64 db;\n\t"
-        "mov.b64 db, {%2, %3};\n\t"
-        "setp.ne.b32 p, %5, 0;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], [%1], db, %4, p;\n\t}"
-        ::"r"(d_tmem), "r"(a_tmem), "r"(b_lo), "r"(hi), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
 // Two MMA threads of the even CTA, on different SM sub-partitions, split the
 // issue work: warp 1 issues every QK, warp 3 every PV, g running over the
 // tiles of all items of this pair.  They share no tensor memory (QK writes S;
@@ -466,18 +276,16 @@ __device__ void qk_issuer(const Params& p, uint8_t* smem, const Bars& B, const W
     drain_wait(&B.drain[0], 0);
 }
 
-// O_b = P_g [V8_g | 1] with b = g % 2 (ExpCast, N = 144), or P_g V8_g (N =
-// 128) with b = g % 2.  PV_g
+// O_b = P_g [V8_g | 1] with b = g % 2 (N = 144).  PV_g
 // waits for P_g, for the corrections' read of O_b (tile g - 2) and for its
 // stage.  The commit that signals PV_g done (o_full, to both CTAs) also
 // frees K/V stage g % kStages (QK_g, which read the stage's K, completed
 // before the softmax of tile g began).  The loop is unrolled by the 8
 // stages, so stage and buffer offsets are constants.
-template <bool EXPCAST>
 __device__ void pv_issuer(const Params& p, uint8_t* smem, const Bars& B, const Waiter& wait, uint32_t tmem, int c,
                           int ncl) {
     static_assert(kStages == 8, "the unrolled loop");
-    const uint32_t idesc = idesc_e4m3_f32(2 * kBM, EXPCAST ? kPvN : 128);
+    const uint32_t idesc = idesc_e4m3_f32(2 * kBM, kPvN);
     const uint64_t k64 = smem_desc_k128(smem + kOffStages);
     const uint32_t hi = (uint32_t)(k64 >> 32);
     const uint32_t v0lo = (uint32_t)k64 + (kHalf >> 4);
@@ -516,25 +324,6 @@ __device__ void pv_issuer(const Params& p, uint8_t* smem, const Bars& B, const W
 // [0, 64) of its row and lane t + 16 columns [64, 128), so the partial row
 // maxima meet in one shuffle.
 
-// 16 TMEM lanes x 32 columns per half: thread t < 16 reads lane base + t at
-// columns [c, c + 32), thread t + 16 the same lane at [c + 64, c + 96)
-// (tcgen05 .16x32bx2 with a half split of 64 columns).
-template <int OFF, int N>
-__device__ __forceinline__ void tmem_ld16x2_at(uint32_t taddr, uint32_t (&r)[N]) {
-    static_assert(OFF + 32 <= N, "range");
-    asm volatile(
-        "tcgen05.ld.sync.aligned.16x32bx2.x32.b32 "
-        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32], 64;"
-        : "=r"(r[OFF + 0]), "=r"(r[OFF + 1]), "=r"(r[OFF + 2]), "=r"(r[OFF + 3]), "=r"(r[OFF + 4]),
-          "=r"(r[OFF + 5]), "=r"(r[OFF + 6]), "=r"(r[OFF + 7]), "=r"(r[OFF + 8]), "=r"(r[OFF + 9]),
-          "=r"(r[OFF + 10]), "=r"(r[OFF + 11]), "=r"(r[OFF + 12]), "=r"(r[OFF + 13]), "=r"(r[OFF + 14]),
-          "=r"(r[OFF + 15]), "=r"(r[OFF + 16]), "=r"(r[OFF + 17]), "=r"(r[OFF + 18]), "=r"(r[OFF + 19]),
-          "=r"(r[OFF + 20]), "=r"(r[OFF + 21]), "=r"(r[OFF + 22]), "=r"(r[OFF + 23]), "=r"(r[OFF + 24]),
-          "=r"(r[OFF + 25]), "=r"(r[OFF + 26]), "=r"(r[OFF + 27]), "=r"(r[OFF + 28]), "=r"(r[OFF + 29]),
-          "=r"(r[OFF + 30]), "=r"(r[OFF + 31])
-        : "r"(taddr));
-}
 // thread t < 16: lane base + t, columns [c, c + 16); thread t + 16: the same
 // lane, columns [c + 16, c + 32): one row's 128 codes in 32 columns
 __device__ __forceinline__ void tmem_st16x2_16(uint32_t taddr, const uint32_t (&r)[16]) {
@@ -545,7 +334,7 @@ __device__ __forceinline__ void tmem_st16x2_16(uint32_t taddr, const uint32_t (&
           "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
         : "memory");
 }
-template <bool EXPCAST, bool PROBE>
+template <bool PROBE>
 __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, const Waiter& wait, uint32_t tmem,
                              uint32_t rank, int c, int ncl, int quarter, int sub, int lane) {
     // warp (quarter, sub) owns rows quarter*32 + sub*16 + [0, 16); lanes t and
@@ -553,7 +342,6 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, cons
     const int hs = lane >> 4;
     const int row = quarter * 32 + sub * 16 + (lane & 15);
     float* st_alpha = reinterpret_cast<float*>(smem + kOffStats);
-    float* st_mass = st_alpha + kStatSlots * 128;               // [kStatSlots][128]
     const uint32_t lead_p = peer_addr(B.p_full, 0);            // p_full[b] at + 8 b
     const uint32_t lead_s = peer_addr(B.s_free, 0);
     const uint32_t trow = tmem + ((uint32_t)(quarter * 32 + sub * 16) << 16);
@@ -620,24 +408,17 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, cons
             // FP32 ulps from expf, inside the output tolerance, and exactly 1
             // when the maximum did not move (the correction skips its rescale then)
             const float alpha = ex2_ftz(__fmul_rn(m - m_new, kLog2e));
-            float A, Bc;
             // A is kept at or above the smallest normal float: a masked key (-inf)
             // times A must stay -inf (code 0, no mass), never -inf * 0 = NaN.  When
             // c underflows that far, every logit s * c is below 2^-100 and the
-            // codes come out as for A = 0, as in the reference.
-            if (EXPCAST) {
-                // in units of 2^-24 throughout: scaling by a power of two is exact,
-                // so this is the unscaled computation times 2^-24, bit for bit
-                A = fmaxf(__fmul_rn(cs, kC1 * kTwoM24), kMinNormal);
-                Bc = __fsub_rn(kC2 * kTwoM24, __fmul_rn(m_new, kC1 * kTwoM24));
-                const float umax = fmaf(rmax, A, Bc);
-                if (umax > 120.25f * kTwoM24) Bc = __fsub_rn(Bc, __fsub_rn(umax, kC2 * kTwoM24));
-            } else {
-                A = fmaxf(__fmul_rn(cs, kLog2e), kMinNormal);
-                Bc = __fsub_rn(8.0f, __fmul_rn(m_new, kLog2e));
-            }
+            // codes come out as for A = 0, as in the reference.  In units of
+            // 2^-24 throughout: scaling by a power of two is exact, so this is
+            // the unscaled computation times 2^-24, bit for bit.
+            const float A = fmaxf(__fmul_rn(cs, kC1 * kTwoM24), kMinNormal);
+            float Bc = __fsub_rn(kC2 * kTwoM24, __fmul_rn(m_new, kC1 * kTwoM24));
+            const float umax = fmaf(rmax, A, Bc);
+            if (umax > 120.25f * kTwoM24) Bc = __fsub_rn(Bc, __fsub_rn(umax, kC2 * kTwoM24));
             const float2 AA = make_float2(A, A), BB = make_float2(Bc, Bc);
-            float ms[4] = {0.0f, 0.0f, 0.0f, 0.0f};   // exp: the FP32 row mass of sum(p * 256)
             uint32_t pk[16];
 #pragma unroll
             for (int w = 0; w < 16; ++w) {
@@ -645,27 +426,12 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, cons
                     ffma2(make_float2(__uint_as_float(r[4 * w]), __uint_as_float(r[4 * w + 1])), AA, BB);
                 const float2 g23 =
                     ffma2(make_float2(__uint_as_float(r[4 * w + 2]), __uint_as_float(r[4 * w + 3])), AA, BB);
-                if (EXPCAST) {
-                    const uint32_t h01 = cvt_relu_f16x2(g01.y, g01.x);   // integer codes as f16 subnormals
-                    const uint32_t h23 = cvt_relu_f16x2(g23.y, g23.x);
-                    pk[w] = __byte_perm(h01, h23, 0x6420);
-                } else {
-                    const float e0 = ex2_ftz(g01.x), e1 = ex2_ftz(g01.y), e2 = ex2_ftz(g23.x), e3 = ex2_ftz(g23.y);
-                    // packed adds: each lane is the same round-to-nearest FP32 add
-                    const float2 s01 = fadd2(make_float2(ms[0], ms[1]), make_float2(e0, e1));
-                    const float2 s23 = fadd2(make_float2(ms[2], ms[3]), make_float2(e2, e3));
-                    ms[0] = s01.x; ms[1] = s01.y; ms[2] = s23.x; ms[3] = s23.y;
-                    pk[w] = e4m3x2(e0, e1) | (e4m3x2(e2, e3) << 16);
-                }
+                const uint32_t h01 = cvt_relu_f16x2(g01.y, g01.x);   // integer codes as f16 subnormals
+                const uint32_t h23 = cvt_relu_f16x2(g23.y, g23.x);
+                pk[w] = __byte_perm(h01, h23, 0x6420);
             }
-            // ExpCast's row mass is the sum of the decoded P, which the PV MMA
-            // forms in its ones columns.  The exp mode keeps the FP32 sum of the
-            // unrounded p * 256; the row's two halves add up to M.
-            float M = 0.0f;
-            if (!EXPCAST) {
-                const float Mh = __fadd_rn(__fadd_rn(ms[0], ms[1]), __fadd_rn(ms[2], ms[3]));
-                M = __fadd_rn(Mh, __shfl_xor_sync(0xffffffffu, Mh, 16));
-            }
+            // The row mass, the sum of the decoded P, is formed by the PV MMA
+            // in its ones columns.
             if (probe && j >= p.pr_begin && j < p.pr_begin + p.pr_count) {
                 const int64_t t = j - p.pr_begin;
                 float* lg = p.pr_logits + (t * 128 + row) * 128 + hs * 64;
@@ -682,10 +448,7 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, cons
             // P_g into P_b: 4 codes per 32-bit column, the A-operand layout of
             // the PV MMA (K slice kk of 32 keys in columns [8 kk, 8 kk + 8))
             tmem_st16x2_16(trow + (b ? kColP1 : kColP0), pk);
-            if (hs == 0) {
-                st_alpha[slot * 128 + row] = alpha;
-                if (!EXPCAST) st_mass[slot * 128 + row] = M;
-            }
+            if (hs == 0) st_alpha[slot * 128 + row] = alpha;
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
@@ -696,26 +459,17 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, cons
     }
 }
 
-// One TMEM column of the warp's 32 lanes: thread i gets lane i.
-__device__ __forceinline__ uint32_t tmem_ld32_x1(uint32_t taddr) {
-    uint32_t r;
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr));
-    return r;
-}
-
 // Two threads per row (warp (quarter, half): rows quarter * 32 + lane,
 // channels half * 64 + [0, 64)).  Per tile, in units of 256 as the softmax:
 // acc = alpha acc + (PV + M mu / vscale) vscale (core.py:335-336: rowmass
 // times the stored scaled mean, then the scale), den = alpha den + M.
-// ExpCast reads M from the mass column of O_b; the exp mode from the
-// softmax's statistics ring.  O_b is released (o_free) once both chunks of
+// M is the mass column of O_b.  O_b is released (o_free) once both chunks of
 // it are in registers.
-template <bool EXPCAST, bool HAS_MEAN>
+template <bool HAS_MEAN>
 __device__ void correction_role(const Params& p, uint8_t* smem, const Bars& B, const Waiter& wait, uint32_t tmem,
                                 uint32_t rank, int c, int ncl, int quarter, int half, int lane) {
     const int row = quarter * 32 + lane;
     const float* st_alpha = reinterpret_cast<const float*>(smem + kOffStats);
-    const float* st_mass = st_alpha + kStatSlots * 128;
     const uint32_t lead_o = peer_addr(B.o_free, 0);            // o_free[b] at + 8 b
     const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
     const int c0 = half * 64;
@@ -734,7 +488,7 @@ __device__ void correction_role(const Params& p, uint8_t* smem, const Bars& B, c
                 return;
             tc_fence_after();
             const float alpha = st_alpha[slot * 128 + row];
-            float M = EXPCAST ? 0.0f : st_mass[slot * 128 + row];
+            float M = 0.0f;
             __syncwarp();
             mbar_arrive_if(&B.st_free[slot], lane == 0);
             const float4* vsp = reinterpret_cast<const float4*>(smem + kOffMeta + s * kMetaBytes);
@@ -751,9 +505,9 @@ __device__ void correction_role(const Params& p, uint8_t* smem, const Bars& B, c
                 uint32_t o[32];
                 tmem_ld32_at<0>(ob + c0 + 32 * ch, o);
                 uint32_t mraw = 0;
-                if (EXPCAST && ch == 0) mraw = tmem_ld32_x1(ob + kColMass);
+                if (ch == 0) mraw = tmem_ld32_x1(ob + kColMass);
                 tmem_wait_ld();
-                if (EXPCAST && ch == 0) M = __uint_as_float(mraw);
+                if (ch == 0) M = __uint_as_float(mraw);
                 if (ch == 1) {
                     tc_fence_before();
                     __syncwarp();
@@ -808,7 +562,7 @@ __device__ void correction_role(const Params& p, uint8_t* smem, const Bars& B, c
     }
 }
 
-template <bool EXPCAST, bool HAS_MEAN, bool PROBE>
+template <bool HAS_MEAN, bool PROBE>
 __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant__ Params p) {
     // The swizzled TMA/MMA layouts need a 1024-byte aligned base; the kernel
     // declares no static shared memory, so the dynamic window starts aligned.
@@ -852,7 +606,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
         *abort = 0;
         fence_barrier_init();
     }
-    if (EXPCAST && rank == 1) {
+    if (rank == 1) {
         // the odd CTA's constant B rows 56..71 of every stage: E4M3 1.0 (0x38)
         // in every byte, so the 128-byte swizzle needs no care; written before
         // the cluster barrier, and made visible to the tensor cores' (async)
@@ -881,16 +635,16 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
     // correction groups 112; 10240 + 22528 + 28672 = 61440.
     if (warp < 4) {
         reg_dealloc<80>();
-        if (warp == 0 && lane == 0) producer<EXPCAST>(p, smem, B, wait, rank, c, ncl);
+        if (warp == 0 && lane == 0) producer(p, smem, B, wait, rank, c, ncl);
         if (warp == 1 && lane == 0 && rank == 0) qk_issuer(p, smem, B, wait, tmem, c, ncl);
-        if (warp == 3 && lane == 0 && rank == 0) pv_issuer<EXPCAST>(p, smem, B, wait, tmem, c, ncl);
+        if (warp == 3 && lane == 0 && rank == 0) pv_issuer(p, smem, B, wait, tmem, c, ncl);
         if (warp == 2 && lane == 0) meta_producer<HAS_MEAN>(p, smem, B, wait, c, ncl);
     } else if (warp < 12) {
         reg_dealloc<88>();
-        softmax_role<EXPCAST, PROBE>(p, smem, B, wait, tmem, rank, c, ncl, warp & 3, (warp - 4) >> 2, lane);
+        softmax_role<PROBE>(p, smem, B, wait, tmem, rank, c, ncl, warp & 3, (warp - 4) >> 2, lane);
     } else {
         reg_alloc<112>();
-        correction_role<EXPCAST, HAS_MEAN>(p, smem, B, wait, tmem, rank, c, ncl, warp & 3, (warp - 12) >> 2, lane);
+        correction_role<HAS_MEAN>(p, smem, B, wait, tmem, rank, c, ncl, warp & 3, (warp - 12) >> 2, lane);
     }
     tc_fence_before();
     __syncwarp();
@@ -904,75 +658,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
     if (threadIdx.x == 0 && *abort) flag_status(p.status, VCB_FLAG_TIMEOUT);
 }
 
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-int get_encoder(EncodeTiledFn* fn) {
-    static EncodeTiledFn cached = nullptr;
-    if (!cached) {
-        void* ptr = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q);
-        if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !ptr)
-            return fail(VCB_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
-        cached = reinterpret_cast<EncodeTiledFn>(ptr);
-    }
-    *fn = cached;
-    return VCB_OK;
-}
-
-// 3-D byte tensor [planes][rows][width] with `width`-byte rows, boxes of
-// width x box_rows, swizzled to the row width (128 B or 32 B).
-int make_map(CUtensorMap* map, const void* base, uint64_t width, uint64_t rows, uint64_t planes, uint32_t box_rows) {
-    EncodeTiledFn enc;
-    int rc = get_encoder(&enc);
-    if (rc) return rc;
-    const cuuint64_t dims[3] = {width, rows, planes};
-    const cuuint64_t strides[2] = {width, width * rows};
-    const cuuint32_t box[3] = {(cuuint32_t)width, box_rows, 1};
-    const cuuint32_t estr[3] = {1, 1, 1};
-    const CUtensorMapSwizzle sw = width == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_32B;
-    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return fail(VCB_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
-    return VCB_OK;
-}
-
-template <bool E, bool M, bool P>
+template <bool M, bool P>
 int launch(const Params& p, cudaStream_t st) {
-    auto kernel = attn_kernel<E, M, P>;
-    VCB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemAlloc));
-    cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = kSmemAlloc;
-    cfg.stream = st;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    // as many pairs as are resident at once (looked up once per device)
-    int dev = 0;
-    VCB_CUDA(cudaGetDevice(&dev));
     static int max_clusters[64][8] = {};
-    const int variant = (E ? 4 : 0) | (M ? 2 : 0) | (P ? 1 : 0);
-    if (dev < 0 || dev >= 64) return fail(VCB_ERR_INVALID_ARGUMENT, "device ordinal %d out of range", dev);
-    int& ncl_max = max_clusters[dev][variant];
-    if (ncl_max == 0) {
-        cfg.gridDim = dim3(2 * 148);
-        int n = 0;
-        VCB_CUDA(cudaOccupancyMaxActiveClusters(&n, kernel, &cfg));
-        if (n < 1) return fail(VCB_ERR_CUDA, "the attention kernel's CTA pairs do not fit on this GPU");
-        ncl_max = n;
-    }
-    const int ncl = p.items < ncl_max ? p.items : ncl_max;
-    cfg.gridDim = dim3(2 * ncl);
-    VCB_CUDA(cudaLaunchKernelEx(&cfg, kernel, p));
-    return VCB_OK;
+    return launch_pairs(attn_kernel<M, P>, p, p.items, kThreads, kSmemAlloc, max_clusters, (M ? 2 : 0) | (P ? 1 : 0),
+                        st);
 }
 
 // Self-test of the bounded waits, with no GPU fault involved.  One CTA sets up
@@ -1034,7 +724,10 @@ __global__ void __launch_bounds__(128, 1)
 
 }  // namespace
 
+// The ExpCast modes run here; the exp modes (fp8_control, v_smooth) on the
+// kernel of vcb_attn_exp.cu, whose softmax forms the FP32 row mass itself.
 int attn_run(const vcb_attn_args* a, const vcb_attn_probe* probe, cudaStream_t st) {
+    if (!a->expcast) return attn_exp_run(a, probe, st);
     Params p;
     memset(&p, 0, sizeof(p));
     const int64_t sq_pad = vcb_padded_rows(a->sq, a->q_block);
@@ -1049,9 +742,8 @@ int attn_run(const vcb_attn_args* a, const vcb_attn_probe* probe, cudaStream_t s
         return fail(VCB_ERR_INVALID_ARGUMENT, "problem too large for the attention kernel's tile counters");
     int rc = make_map(&p.tm_q, a->q8, 128, (uint64_t)sq_pad, (uint64_t)a->heads, kBM);
     if (!rc) rc = make_map(&p.tm_k, a->k8, 128, (uint64_t)sk_pad, (uint64_t)a->heads, 64);
-    const uint32_t v_rows0 = a->expcast ? kVRows0 : 64, v_rows1 = a->expcast ? kVRows1 : 64;
-    if (!rc) rc = make_map(&p.tm_v0, a->v8, 128, (uint64_t)T * 128, (uint64_t)a->heads, v_rows0);
-    if (!rc) rc = make_map(&p.tm_v1, a->v8, 128, (uint64_t)T * 128, (uint64_t)a->heads, v_rows1);
+    if (!rc) rc = make_map(&p.tm_v0, a->v8, 128, (uint64_t)T * 128, (uint64_t)a->heads, kVRows0);
+    if (!rc) rc = make_map(&p.tm_v1, a->v8, 128, (uint64_t)T * 128, (uint64_t)a->heads, kVRows1);
     if (rc) return rc;
     p.q_scale = a->q_scale;
     p.k_scale = a->k_scale;
@@ -1078,12 +770,9 @@ int attn_run(const vcb_attn_args* a, const vcb_attn_probe* probe, cudaStream_t s
         p.pr_qtile = (int)probe->q_tile;
         p.pr_begin = probe->tile_begin;
         p.pr_count = probe->tile_count;
-        if (a->expcast)
-            return a->has_mean ? launch<true, true, true>(p, st) : launch<true, false, true>(p, st);
-        return a->has_mean ? launch<false, true, true>(p, st) : launch<false, false, true>(p, st);
+        return a->has_mean ? launch<true, true>(p, st) : launch<false, true>(p, st);
     }
-    if (a->expcast) return a->has_mean ? launch<true, true, false>(p, st) : launch<true, false, false>(p, st);
-    return a->has_mean ? launch<false, true, false>(p, st) : launch<false, false, false>(p, st);
+    return a->has_mean ? launch<true, false>(p, st) : launch<false, false>(p, st);
 }
 
 int wait_selftest_run(int complete, const void* src, int32_t* status, int32_t* report, cudaStream_t st) {

@@ -16,9 +16,13 @@ int vprep_run(const vcb_v_args* p, cudaStream_t st);
 size_t group_workspace_bytes(int64_t heads, int64_t s, int d, int clusters);
 int group_run(const vcb_group_args* p, cudaStream_t st);
 
-// vcb_attn.cu
+// vcb_api.cu: the SM count of the current device (cached)
 int sm_count();
+
+// vcb_attn.cu (ExpCast modes; dispatches the others to vcb_attn_exp.cu)
 int attn_run(const vcb_attn_args* p, const vcb_attn_probe* probe, cudaStream_t st);
+// vcb_attn_exp.cu (exp modes: fp8_control, v_smooth)
+int attn_exp_run(const vcb_attn_args* p, const vcb_attn_probe* probe, cudaStream_t st);
 int wait_selftest_run(int complete, const void* src, int32_t* status, int32_t* report, cudaStream_t st);
 
 // vcb_expcast.cu

@@ -41,6 +41,14 @@ def test_padded_rows_and_workspace_sizes():
     ws = lib.vcb_forward_workspace(ctypes.byref(a))
     # q8 + k8 + v8 (1 byte each) + scales + V metadata + K-mean scratch
     assert 3 * 40 * 32768 * 128 < ws < 3 * 40 * 32768 * 128 * 1.1
+    # the bf16 mean operand [heads, T, 128, 16] is laid out only for V-Smooth
+    # in the exp modes; the ExpCast kernel reads the means from v_meta
+    sizes = {}
+    for smooth, expcast in ((0, 0), (1, 0), (0, 1), (1, 1)):
+        a.smooth, a.expcast = smooth, expcast
+        sizes[smooth, expcast] = lib.vcb_forward_workspace(ctypes.byref(a))
+    assert sizes[1, 0] - sizes[0, 0] == 40 * 256 * 128 * 16 * 2
+    assert sizes[1, 1] == sizes[0, 1] == sizes[0, 0]
 
 
 @pytest.mark.parametrize("field,value,match", [

@@ -265,8 +265,9 @@ int vcb_attention_fp8(const vcb_attn_args* a, void* stream) {
 }
 
 // Workspace of vcb_forward, carved in this order (256-byte aligned pieces):
-// q8, k8, q_scale, k_scale, v8, v_meta, the V-mean operand, then the Q/K-prep
-// scratch.
+// q8, k8, q_scale, k_scale, v8, v_meta, the V-mean operand (V-Smooth in the
+// exp modes only: the ExpCast kernel reads the means from v_meta), then the
+// Q/K-prep scratch.
 namespace {
 struct ForwardLayout {
     size_t q8, k8, qs, ks, v8, vm, mop, qk, total;
@@ -284,7 +285,7 @@ ForwardLayout forward_layout(const vcb_forward_args* a) {
     L.ks = o; o += r((size_t)(a->heads * ((a->sk + a->k_quant_block - 1) / a->k_quant_block)) * 4);
     L.v8 = o; o += r((size_t)(a->heads * T * 128 * 128));
     L.vm = o; o += r((size_t)(a->heads * T * 256) * 4);
-    L.mop = o; o += a->smooth ? r((size_t)(a->heads * T * 128 * 16) * 2) : 0;
+    L.mop = o; o += (a->smooth && !a->expcast) ? r((size_t)(a->heads * T * 128 * 16) * 2) : 0;
     L.qk = o; o += r(qk_workspace_bytes(a->heads, a->sk));
     L.total = o;
     return L;
@@ -331,7 +332,7 @@ int vcb_forward(const vcb_forward_args* a, void* stream) {
     va.v = a->v; va.dtype = a->dtype; va.heads = a->heads; va.s = a->sk; va.dv = a->dv; va.pi = a->pi;
     va.active = a->smooth; va.mean_type = a->mean_type; va.kv_block = a->kv_block;
     va.v8 = reinterpret_cast<uint8_t*>(ws + L.v8); va.v_meta = reinterpret_cast<float*>(ws + L.vm);
-    va.v_mean_op = a->smooth ? reinterpret_cast<uint16_t*>(ws + L.mop) : nullptr;
+    va.v_mean_op = (a->smooth && !a->expcast) ? reinterpret_cast<uint16_t*>(ws + L.mop) : nullptr;
     va.status = a->status;
     VCB_REQUIRE(a->dv >= 1 && a->dv <= 128, "value dimension must be in [1, 128]");
 

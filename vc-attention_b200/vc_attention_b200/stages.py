@@ -39,16 +39,18 @@ def quantize_qk(q, k, *, pi=None, q_block=128, k_quant_block=256, k_smooth=True,
     return q8, qs, k8, ks
 
 
-def prepare_v(v, *, pi=None, active=True, mean_dtype="float16", kv_block=128, status=None):
+def prepare_v(v, *, pi=None, active=True, mean_dtype="float16", kv_block=128, status=None, mean_op=True):
     """vcb_prepare_v: returns (v8 [BH, T, 128, 128] u8, v_meta [BH, T, 2, 128] f32,
-    mean_op [BH, T, 128, 16] bf16 as uint16, or None when not active)."""
+    mean_op [BH, T, 128, 16] bf16 as uint16, or None when not active or not
+    asked for: only the exp-mode attention kernel reads it, the ExpCast one
+    takes the means from v_meta)."""
     lib = _extension()
     b, h, s, dv = v.shape
     heads = b * h
     t = -(-s // kv_block)
     v8 = torch.empty((heads, t, 128, kv_block), dtype=torch.uint8, device=v.device)
     meta = torch.empty((heads, t, 2, 128), dtype=torch.float32, device=v.device)
-    mop = torch.empty((heads, t, 128, 16), dtype=torch.int16, device=v.device) if active else None
+    mop = torch.empty((heads, t, 128, 16), dtype=torch.int16, device=v.device) if active and mean_op else None
     vf = _flat(v)
     a = _abi.VArgs(v=vf.data_ptr(), dtype=_DTYPES[v.dtype], heads=heads, s=s, dv=dv, pi=_i(pi), active=int(active),
                    mean_type=_MEAN_TYPES[mean_dtype], kv_block=kv_block, v8=v8.data_ptr(), v_meta=meta.data_ptr(),
@@ -71,7 +73,7 @@ def _attn_args(q8, qs, k8, ks, v8, meta, mop, out, *, heads, sq, sk, dv, q_block
 def attention_fp8(q8, qs, k8, ks, v8, meta, *, heads, sq, sk, dv, mean_op=None, q_block=128, k_quant_block=256,
                   expcast=True, has_mean=True, scale, out_dtype=torch.bfloat16, out=None, status=None):
     """vcb_attention_fp8 on prepared operands (mean_op: the third output of
-    prepare_v, needed with has_mean); returns [heads, sq, dv]."""
+    prepare_v, needed with has_mean when not expcast); returns [heads, sq, dv]."""
     lib = _extension()
     if out is None:
         out = torch.empty((heads, sq, dv), dtype=out_dtype, device=q8.device)

@@ -483,8 +483,10 @@ __device__ void correction_role(const Params& p, uint8_t* smem, const Bars& B, c
         float den = 0.0f;
         for (int j = 0; j < p.T; ++j, ++g) {
             const uint32_t b = g & 1, slot = g % kStatSlots, s = g % kMetaSlots;
-            if (!wait.all(&B.o_full[b], (g >> 1) & 1, &B.st_full[slot], (g / kStatSlots) & 1, &B.meta_full[s],
-                          (g / kMetaSlots) & 1))
+            // without V-Smooth the correction has slack enough to park in its
+            // waits, which leaves their issue slots to the softmax warps
+            if (!wait.all_or_parked<!HAS_MEAN>(&B.o_full[b], (g >> 1) & 1, &B.st_full[slot], (g / kStatSlots) & 1,
+                                               &B.meta_full[s], (g / kMetaSlots) & 1))
                 return;
             tc_fence_after();
             const float alpha = st_alpha[slot * 128 + row];

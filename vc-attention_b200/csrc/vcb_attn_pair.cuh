@@ -148,6 +148,16 @@ struct Waiter {
         }
         return true;
     }
+    // all() for a role off the critical path: parks in each incomplete phase
+    __device__ __forceinline__ bool parked_all(uint64_t* b0, uint32_t p0, uint64_t* b1, uint32_t p1,
+                                               uint64_t* b2 = nullptr, uint32_t p2 = 0) const {
+        return parked(b0, p0) && (!b1 || parked(b1, p1)) && (!b2 || parked(b2, p2));
+    }
+    template <bool PARK>
+    __device__ __forceinline__ bool all_or_parked(uint64_t* b0, uint32_t p0, uint64_t* b1, uint32_t p1,
+                                                  uint64_t* b2 = nullptr, uint32_t p2 = 0) const {
+        return PARK ? parked_all(b0, p0, b1, p1, b2, p2) : all(b0, p0, b1, p1, b2, p2);
+    }
 };
 
 // 2^x as the single MUFU.EX2 instruction, flushing subnormal results to zero.

@@ -17,20 +17,19 @@
 // a time.  Barrier phases run on across items; the prologue and epilogue of
 // consecutive items overlap.
 //
-// Roles per CTA (640 threads, register budgets rebalanced with setmaxnreg):
+// Roles per CTA (512 threads, register budgets rebalanced with setmaxnreg):
 //   warp 0      TMA producer: this CTA's Q tile of each item (2 buffers),
 //               then its share of K / V tiles into an 8-stage ring.
-//   warps 1, 3  MMA issuers (even CTA, one thread each; warp 1 takes the
-//               even tiles g and buffer S0, warp 3 the odd ones and S1):
-//               S_g = Q8 K8_g^T and O = P_g [V8_g | 1], all with
-//               cta_group::2.
+//   warp 1      QK issuer (even CTA, one thread): S_g = Q8 K8_g^T into the
+//               one S buffer once the softmax has read S_{g-1}.
+//   warp 3      PV issuer (even CTA, one thread): O_b = P_g [V8_g | 1],
+//               b = g % 2; both with cta_group::2.
 //   warp 2      the per-tile V scales and stored means into a 16-slot ring.
-//   warps 4-11  softmax, two threads of one warp per query row (64 scores
-//               each): row max, alpha, the ExpCast encode (one packed FMA per
-//               pair of scores; the f16-subnormal conversion rounds to the
-//               integer code and clamps it at zero) or exp + E4M3(p * 256)
-//               with its FP32 row mass; P_g back over its own S_g columns.
-//   warps 12-19 correction, two threads per row (64 channels each):
+//   warps 4-7   softmax, one thread per query row (128 scores): row max,
+//               alpha, the ExpCast encode (one packed FMA per pair of
+//               scores; the f16-subnormal conversion rounds to the integer
+//               code and clamps it at zero); P_g into P_b.
+//   warps 8-15  correction, two threads per row (64 channels each):
 //               acc = alpha acc + (O + M mu) vscale, den = alpha den + M;
 //               epilogue acc / den in the output dtype after each item.
 //
@@ -66,7 +65,7 @@ namespace {
 
 constexpr int kStages = 8;
 constexpr int kMetaSlots = 16;                    // per-tile vscale ring
-constexpr int kThreads = 640;                     // 20 warps: 4 producer/MMA, 8 softmax, 8 correction
+constexpr int kThreads = 512;                     // 16 warps: 4 producer/MMA, 4 softmax, 8 correction
 // The PV MMA's B operand: 72 rows of 128 keys in each CTA (N = 144).  The
 // even CTA loads V channels 0..71, the odd CTA channels 72..127 into rows
 // 0..55 and keeps E4M3 ones in rows 56..71, so O columns 0..127 are the 128
@@ -324,27 +323,30 @@ __device__ void pv_issuer(const Params& p, uint8_t* smem, const Bars& B, const W
 // [0, 64) of its row and lane t + 16 columns [64, 128), so the partial row
 // maxima meet in one shuffle.
 
-// thread t < 16: lane base + t, columns [c, c + 16); thread t + 16: the same
-// lane, columns [c + 16, c + 32): one row's 128 codes in 32 columns
-__device__ __forceinline__ void tmem_st16x2_16(uint32_t taddr, const uint32_t (&r)[16]) {
+// 32 TMEM lanes x 32 consecutive columns from r[0 .. 31]: thread i writes
+// lane i (one row's 128 P codes, 4 per column).
+__device__ __forceinline__ void tmem_st32_x32(uint32_t taddr, const uint32_t (&r)[32]) {
     asm volatile(
-        "tcgen05.st.sync.aligned.16x32bx2.x16.b32 [%0], 16, {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
-        "%13, %14, %15, %16};"
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
+        "%13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};"
         ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
-          "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+          "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
+          "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
+          "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
         : "memory");
 }
+
+// One thread per query row: warp `quarter` owns rows quarter * 32 + lane and
+// reads all 128 scores of its row, so the row maximum needs no exchange and
+// the per-tile scalar work, waits and arrivals run in four warps per CTA.
 template <bool PROBE>
 __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, const Waiter& wait, uint32_t tmem,
-                             uint32_t rank, int c, int ncl, int quarter, int sub, int lane) {
-    // warp (quarter, sub) owns rows quarter*32 + sub*16 + [0, 16); lanes t and
-    // t + 16 share row t, columns [0, 64) and [64, 128)
-    const int hs = lane >> 4;
-    const int row = quarter * 32 + sub * 16 + (lane & 15);
+                             uint32_t rank, int c, int ncl, int quarter, int lane) {
+    const int row = quarter * 32 + lane;
     float* st_alpha = reinterpret_cast<float*>(smem + kOffStats);
     const uint32_t lead_p = peer_addr(B.p_full, 0);            // p_full[b] at + 8 b
     const uint32_t lead_s = peer_addr(B.s_free, 0);
-    const uint32_t trow = tmem + ((uint32_t)(quarter * 32 + sub * 16) << 16);
+    const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
     const int kstep = p.kq / kBN;
     uint32_t g = 0;
     for (int it = c; it < p.items; it += ncl) {
@@ -365,7 +367,6 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, cons
                 kcnt = 0;
                 ++kidx;
             }
-            const uint32_t ts = trow + kColS;
             const int slot = g % kStatSlots;
             // the scores of tile g, and (checked alongside) the statistics
             // slot this tile writes at its end and the completion of PV_{g-2},
@@ -375,33 +376,33 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, cons
                           g >= 2 ? &B.o_full[b] : nullptr, ((g - 2) >> 1) & 1))
                 return;
             tc_fence_after();
-            uint32_t r[64];
-            tmem_ld16x2_at<0>(ts, r);
-            tmem_ld16x2_at<32>(ts + 32, r);
+            uint32_t r[128];
+            tmem_ld32_at<0>(trow + kColS, r);
+            tmem_ld32_at<32>(trow + kColS + 32, r);
+            tmem_ld32_at<64>(trow + kColS + 64, r);
+            tmem_ld32_at<96>(trow + kColS + 96, r);
             tmem_wait_ld();
             // S is in registers: QK_{g+1} may overwrite it
             tc_fence_before();
             __syncwarp();
             mbar_arrive_cluster_if(lead_s, lane == 0);
             if (j == p.T - 1) {             // only the last tile of an item can be partial
-                const int nvalid = (int)(p.sk - (int64_t)j * kBN) - 64 * hs;
-                if (nvalid < 64) {
+                const int nvalid = (int)(p.sk - (int64_t)j * kBN);
+                if (nvalid < 128) {
 #pragma unroll
-                    for (int i = 0; i < 64; ++i)
+                    for (int i = 0; i < 128; ++i)
                         if (i >= nvalid) r[i] = 0xff800000u;   // -inf: masked key
                 }
             }
-            float mx[4];
+            float mx[8];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) mx[k] = fmaxf(__uint_as_float(r[2 * k]), __uint_as_float(r[2 * k + 1]));
+            for (int k = 0; k < 8; ++k) mx[k] = fmaxf(__uint_as_float(r[2 * k]), __uint_as_float(r[2 * k + 1]));
 #pragma unroll
             for (int t = 1; t < 8; ++t)
 #pragma unroll
-                for (int k = 0; k < 4; ++k)
-                    mx[k] = fmax3(mx[k], __uint_as_float(r[8 * t + 2 * k]), __uint_as_float(r[8 * t + 2 * k + 1]));
-            const float pmax = fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]);
-            const float omax = __shfl_xor_sync(0xffffffffu, pmax, 16);   // the other half of the row
-            const float rmax = fmaxf(pmax, omax);
+                for (int k = 0; k < 8; ++k)
+                    mx[k] = fmax3(mx[k], __uint_as_float(r[16 * t + 2 * k]), __uint_as_float(r[16 * t + 2 * k + 1]));
+            const float rmax = fmaxf(fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]), mx[6]), mx[7]);
             const float cs = __fmul_rn(__fmul_rn(qs_scale, ks), p.scale);
             const float m_new = fmaxf(m, __fmul_rn(rmax, cs));
             // alpha = e^(m - m_new) as 2^((m - m_new) log2 e) on MUFU.EX2: a few
@@ -419,9 +420,9 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, cons
             const float umax = fmaf(rmax, A, Bc);
             if (umax > 120.25f * kTwoM24) Bc = __fsub_rn(Bc, __fsub_rn(umax, kC2 * kTwoM24));
             const float2 AA = make_float2(A, A), BB = make_float2(Bc, Bc);
-            uint32_t pk[16];
+            uint32_t pk[32];
 #pragma unroll
-            for (int w = 0; w < 16; ++w) {
+            for (int w = 0; w < 32; ++w) {
                 const float2 g01 =
                     ffma2(make_float2(__uint_as_float(r[4 * w]), __uint_as_float(r[4 * w + 1])), AA, BB);
                 const float2 g23 =
@@ -434,21 +435,19 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, cons
             // in its ones columns.
             if (probe && j >= p.pr_begin && j < p.pr_begin + p.pr_count) {
                 const int64_t t = j - p.pr_begin;
-                float* lg = p.pr_logits + (t * 128 + row) * 128 + hs * 64;
-                uint32_t* cd = reinterpret_cast<uint32_t*>(p.pr_codes + (t * 128 + row) * 128 + hs * 64);
+                float* lg = p.pr_logits + (t * 128 + row) * 128;
+                uint32_t* cd = reinterpret_cast<uint32_t*>(p.pr_codes + (t * 128 + row) * 128);
 #pragma unroll
-                for (int i = 0; i < 64; ++i) lg[i] = __uint_as_float(r[i]);
+                for (int i = 0; i < 128; ++i) lg[i] = __uint_as_float(r[i]);
 #pragma unroll
-                for (int w = 0; w < 16; ++w) cd[w] = pk[w];
-                if (hs == 0) {
-                    float* rs = p.pr_rowstat + (t * 128 + row) * 4;
-                    rs[0] = m_new; rs[1] = A; rs[2] = Bc; rs[3] = alpha;
-                }
+                for (int w = 0; w < 32; ++w) cd[w] = pk[w];
+                float* rs = p.pr_rowstat + (t * 128 + row) * 4;
+                rs[0] = m_new; rs[1] = A; rs[2] = Bc; rs[3] = alpha;
             }
             // P_g into P_b: 4 codes per 32-bit column, the A-operand layout of
             // the PV MMA (K slice kk of 32 keys in columns [8 kk, 8 kk + 8))
-            tmem_st16x2_16(trow + (b ? kColP1 : kColP0), pk);
-            if (hs == 0) st_alpha[slot * 128 + row] = alpha;
+            tmem_st32_x32(trow + (b ? kColP1 : kColP0), pk);
+            st_alpha[slot * 128 + row] = alpha;
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
@@ -588,8 +587,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
             mbar_init(&B.q_free[i], 1);           // the QK thread
             mbar_init(&B.drain[i], 1);
             mbar_init(&B.s_full[i], 1);
-            mbar_init(&B.s_free[i], 16);          // 8 softmax warps in each CTA
-            mbar_init(&B.p_full[i], 16);          // 8 softmax warps in each CTA
+            mbar_init(&B.s_free[i], 8);           // 4 softmax warps in each CTA
+            mbar_init(&B.p_full[i], 8);           // 4 softmax warps in each CTA
             mbar_init(&B.o_full[i], 1);
             mbar_init(&B.o_free[i], 16);          // 8 correction warps in each CTA
         }
@@ -602,7 +601,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
             mbar_init(&B.meta_empty[s], 8);
         }
         for (int s = 0; s < kStatSlots; ++s) {
-            mbar_init(&B.st_full[s], 8);
+            mbar_init(&B.st_full[s], 4);
             mbar_init(&B.st_free[s], 8);
         }
         *abort = 0;
@@ -631,22 +630,23 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
     const uint32_t tmem = *tmem_slot;
     const Waiter wait{abort, peer_addr(const_cast<int*>(abort), rank ^ 1u)};
 
-    // Register split of the 640 x 96 launch budget (ptxas allocates each
+    // Register split of the 512 x 128 launch budget (ptxas allocates each
     // role's code within its share): producer/MMA group 80 (the unrolled MMA
-    // loop with its item cursor spills below 72), softmax groups 88,
-    // correction groups 112; 10240 + 22528 + 28672 = 61440.
+    // loop with its item cursor spills below 72), softmax 192 (a row's 128
+    // scores and 32 code words), correction 112; 10240 + 24576 + 28672 =
+    // 63488 of 65536.
     if (warp < 4) {
         reg_dealloc<80>();
         if (warp == 0 && lane == 0) producer(p, smem, B, wait, rank, c, ncl);
         if (warp == 1 && lane == 0 && rank == 0) qk_issuer(p, smem, B, wait, tmem, c, ncl);
         if (warp == 3 && lane == 0 && rank == 0) pv_issuer(p, smem, B, wait, tmem, c, ncl);
         if (warp == 2 && lane == 0) meta_producer<HAS_MEAN>(p, smem, B, wait, c, ncl);
-    } else if (warp < 12) {
-        reg_dealloc<88>();
-        softmax_role<PROBE>(p, smem, B, wait, tmem, rank, c, ncl, warp & 3, (warp - 4) >> 2, lane);
+    } else if (warp < 8) {
+        reg_alloc<192>();
+        softmax_role<PROBE>(p, smem, B, wait, tmem, rank, c, ncl, warp & 3, lane);
     } else {
-        reg_alloc<112>();
-        correction_role<HAS_MEAN>(p, smem, B, wait, tmem, rank, c, ncl, warp & 3, (warp - 12) >> 2, lane);
+        reg_dealloc<112>();
+        correction_role<HAS_MEAN>(p, smem, B, wait, tmem, rank, c, ncl, warp & 3, (warp - 8) >> 2, lane);
     }
     tc_fence_before();
     __syncwarp();

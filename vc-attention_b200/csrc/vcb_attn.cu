@@ -17,7 +17,7 @@
 // a time.  Barrier phases run on across items; the prologue and epilogue of
 // consecutive items overlap.
 //
-// Roles per CTA (512 threads, register budgets rebalanced with setmaxnreg):
+// Roles per CTA (384 threads, register budgets rebalanced with setmaxnreg):
 //   warp 0      TMA producer: this CTA's Q tile of each item (2 buffers),
 //               then its share of K / V tiles into an 8-stage ring.
 //   warp 1      QK issuer (even CTA, one thread): S_g = Q8 K8_g^T into the
@@ -29,7 +29,7 @@
 //               alpha, the ExpCast encode (one packed FMA per pair of
 //               scores; the f16-subnormal conversion rounds to the integer
 //               code and clamps it at zero); P_g into P_b.
-//   warps 8-15  correction, two threads per row (64 channels each):
+//   warps 8-11  correction, one thread per row (128 channels):
 //               acc = alpha acc + (O + M mu) vscale, den = alpha den + M;
 //               epilogue acc / den in the output dtype after each item.
 //
@@ -65,7 +65,7 @@ namespace {
 
 constexpr int kStages = 8;
 constexpr int kMetaSlots = 16;                    // per-tile vscale ring
-constexpr int kThreads = 512;                     // 16 warps: 4 producer/MMA, 4 softmax, 8 correction
+constexpr int kThreads = 384;                     // 12 warps: 4 producer/MMA, 4 softmax, 4 correction
 // The PV MMA's B operand: 72 rows of 128 keys in each CTA (N = 144).  The
 // even CTA loads V channels 0..71, the odd CTA channels 72..127 into rows
 // 0..55 and keeps E4M3 ones in rows 56..71, so O columns 0..127 are the 128
@@ -458,27 +458,26 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, cons
     }
 }
 
-// Two threads per row (warp (quarter, half): rows quarter * 32 + lane,
-// channels half * 64 + [0, 64)).  Per tile, in units of 256 as the softmax:
-// acc = alpha acc + (PV + M mu / vscale) vscale (core.py:335-336: rowmass
-// times the stored scaled mean, then the scale), den = alpha den + M.
-// M is the mass column of O_b.  O_b is released (o_free) once both chunks of
-// it are in registers.
+// One thread per row (warp `quarter`: rows quarter * 32 + lane, all 128
+// channels).  Per tile, in units of 256 as the softmax: acc = alpha acc +
+// (PV + M mu / vscale) vscale (core.py:335-336: rowmass times the stored
+// scaled mean, then the scale), den = alpha den + M, with M the mass column
+// of O_b.  O_b is read in four 32-column chunks and released (o_free) once
+// the last is in registers.
 template <bool HAS_MEAN>
 __device__ void correction_role(const Params& p, uint8_t* smem, const Bars& B, const Waiter& wait, uint32_t tmem,
-                                uint32_t rank, int c, int ncl, int quarter, int half, int lane) {
+                                uint32_t rank, int c, int ncl, int quarter, int lane) {
     const int row = quarter * 32 + lane;
     const float* st_alpha = reinterpret_cast<const float*>(smem + kOffStats);
     const uint32_t lead_o = peer_addr(B.o_free, 0);            // o_free[b] at + 8 b
     const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
-    const int c0 = half * 64;
     uint32_t g = 0;
     for (int it = c; it < p.items; it += ncl) {
         const int head = it / p.pairs, pair = it - head * p.pairs;
         const int64_t grow = (int64_t)(2 * pair + (int)rank) * kBM + row;
-        float2 acc[32];
+        float2 acc[64];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) acc[i] = make_float2(0.0f, 0.0f);
+        for (int i = 0; i < 64; ++i) acc[i] = make_float2(0.0f, 0.0f);
         float den = 0.0f;
         for (int j = 0; j < p.T; ++j, ++g) {
             const uint32_t b = g & 1, slot = g % kStatSlots, s = g % kMetaSlots;
@@ -489,7 +488,6 @@ __device__ void correction_role(const Params& p, uint8_t* smem, const Bars& B, c
                 return;
             tc_fence_after();
             const float alpha = st_alpha[slot * 128 + row];
-            float M = 0.0f;
             __syncwarp();
             mbar_arrive_if(&B.st_free[slot], lane == 0);
             const float4* vsp = reinterpret_cast<const float4*>(smem + kOffMeta + s * kMetaBytes);
@@ -499,17 +497,18 @@ __device__ void correction_role(const Params& p, uint8_t* smem, const Bars& B, c
             const uint32_t ob = trow + (b ? kColO1 : kColO0);
             if (rescale) {      // warp-uniform; alpha == 1 leaves acc unchanged
 #pragma unroll
-                for (int i = 0; i < 32; ++i) acc[i] = fmul2(acc[i], aa);
+                for (int i = 0; i < 64; ++i) acc[i] = fmul2(acc[i], aa);
             }
+            float M = 0.0f;
 #pragma unroll
-            for (int ch = 0; ch < 2; ++ch) {
+            for (int ch = 0; ch < 4; ++ch) {
                 uint32_t o[32];
-                tmem_ld32_at<0>(ob + c0 + 32 * ch, o);
+                tmem_ld32_at<0>(ob + 32 * ch, o);
                 uint32_t mraw = 0;
                 if (ch == 0) mraw = tmem_ld32_x1(ob + kColMass);
                 tmem_wait_ld();
                 if (ch == 0) M = __uint_as_float(mraw);
-                if (ch == 1) {
+                if (ch == 3) {
                     tc_fence_before();
                     __syncwarp();
                     mbar_arrive_cluster_if(lead_o + 8 * b, lane == 0);
@@ -517,12 +516,12 @@ __device__ void correction_role(const Params& p, uint8_t* smem, const Bars& B, c
                 const float2 mm = make_float2(M, M);
 #pragma unroll
                 for (int q = 0; q < 8; ++q) {
-                    const float4 vs = vsp[(c0 >> 2) + 8 * ch + q];
+                    const float4 vs = vsp[8 * ch + q];
                     const int i = 16 * ch + 2 * q;
                     float2 o01 = make_float2(__uint_as_float(o[4 * q]), __uint_as_float(o[4 * q + 1]));
                     float2 o23 = make_float2(__uint_as_float(o[4 * q + 2]), __uint_as_float(o[4 * q + 3]));
                     if (HAS_MEAN) {
-                        const float4 u = usp[(c0 >> 2) + 8 * ch + q];
+                        const float4 u = usp[8 * ch + q];
                         o01 = ffma2(mm, make_float2(u.x, u.y), o01);
                         o23 = ffma2(mm, make_float2(u.z, u.w), o23);
                     }
@@ -537,9 +536,9 @@ __device__ void correction_role(const Params& p, uint8_t* smem, const Bars& B, c
         if (grow >= p.sq) continue;
         const int64_t base = ((int64_t)head * p.sq + grow) * p.dv;
         if (p.out_dtype == VCB_BF16 && p.dv == 128) {
-            uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + base + c0);
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + base);
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
+            for (int q = 0; q < 16; ++q) {
                 uint32_t w[4];
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
@@ -551,14 +550,23 @@ __device__ void correction_role(const Params& p, uint8_t* smem, const Bars& B, c
             }
             continue;
         }
+        // other dtypes or dv < 128: channel by channel (static indices only, so
+        // acc stays in registers)
 #pragma unroll
         for (int i = 0; i < 64; ++i) {
-            const int col = c0 + i;
-            if (col >= p.dv) break;
-            const float val = __fdiv_rn((i & 1) ? acc[i >> 1].y : acc[i >> 1].x, den);
-            if (p.out_dtype == VCB_BF16) static_cast<__nv_bfloat16*>(p.out)[base + col] = __float2bfloat16_rn(val);
-            else if (p.out_dtype == VCB_F16) static_cast<__half*>(p.out)[base + col] = __float2half_rn(val);
-            else static_cast<float*>(p.out)[base + col] = val;
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int col = 2 * i + e;
+                if (col < p.dv) {
+                    const float val = __fdiv_rn(e ? acc[i].y : acc[i].x, den);
+                    if (p.out_dtype == VCB_BF16)
+                        static_cast<__nv_bfloat16*>(p.out)[base + col] = __float2bfloat16_rn(val);
+                    else if (p.out_dtype == VCB_F16)
+                        static_cast<__half*>(p.out)[base + col] = __float2half_rn(val);
+                    else
+                        static_cast<float*>(p.out)[base + col] = val;
+                }
+            }
         }
     }
 }
@@ -590,7 +598,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
             mbar_init(&B.s_free[i], 8);           // 4 softmax warps in each CTA
             mbar_init(&B.p_full[i], 8);           // 4 softmax warps in each CTA
             mbar_init(&B.o_full[i], 1);
-            mbar_init(&B.o_free[i], 16);          // 8 correction warps in each CTA
+            mbar_init(&B.o_free[i], 8);           // 4 correction warps in each CTA
         }
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&B.kv_full[s], 1);
@@ -598,11 +606,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
         }
         for (int s = 0; s < kMetaSlots; ++s) {
             mbar_init(&B.meta_full[s], 1);
-            mbar_init(&B.meta_empty[s], 8);
+            mbar_init(&B.meta_empty[s], 4);
         }
         for (int s = 0; s < kStatSlots; ++s) {
             mbar_init(&B.st_full[s], 4);
-            mbar_init(&B.st_free[s], 8);
+            mbar_init(&B.st_free[s], 4);
         }
         *abort = 0;
         fence_barrier_init();
@@ -630,11 +638,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
     const uint32_t tmem = *tmem_slot;
     const Waiter wait{abort, peer_addr(const_cast<int*>(abort), rank ^ 1u)};
 
-    // Register split of the 512 x 128 launch budget (ptxas allocates each
+    // Register split of the 384 x 168 launch budget (ptxas allocates each
     // role's code within its share): producer/MMA group 80 (the unrolled MMA
     // loop with its item cursor spills below 72), softmax 192 (a row's 128
-    // scores and 32 code words), correction 112; 10240 + 24576 + 28672 =
-    // 63488 of 65536.
+    // scores and 32 code words), correction 192 (a row's 128 accumulators and
+    // one 32-column chunk of O); 10240 + 24576 + 24576 = 59392 of 64512.
     if (warp < 4) {
         reg_dealloc<80>();
         if (warp == 0 && lane == 0) producer(p, smem, B, wait, rank, c, ncl);
@@ -645,8 +653,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
         reg_alloc<192>();
         softmax_role<PROBE>(p, smem, B, wait, tmem, rank, c, ncl, warp & 3, lane);
     } else {
-        reg_dealloc<112>();
-        correction_role<HAS_MEAN>(p, smem, B, wait, tmem, rank, c, ncl, warp & 3, (warp - 8) >> 2, lane);
+        reg_alloc<192>();
+        correction_role<HAS_MEAN>(p, smem, B, wait, tmem, rank, c, ncl, warp & 3, lane);
     }
     tc_fence_before();
     __syncwarp();

@@ -500,7 +500,10 @@ def run_ours(args, world, rank, local):
     # region, so a garbage-collector pause there would stall the GPU
     gc.collect()
     gc.disable()
-    for i in range(args.warmup + args.steps):
+    # at least 20 timed steps (about 0.5 s), so that a few steps stretched by
+    # other load on a shared host cannot move the median
+    e2e_steps = max(args.steps, 20)
+    for i in range(args.warmup + e2e_steps):
         torch.cuda.synchronize()
         barrier(world)
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -547,7 +550,7 @@ def run_ours(args, world, rank, local):
                     "estimator": "median step time, max over ranks of each rank's median",
                     "ms_per_step_mean": e2e_mean,
                     "value_from_mean": flops() / (e2e_mean * 1e-3) / 1e12,
-                    "steps_ms": [round(t, 3) for t in e2e_ms],
+                    "steps_ms": [round(t, 3) for t in e2e_ms], "timed_steps": e2e_steps,
                     "h2d_bytes_per_step": 3 * nbytes, "d2h_bytes_per_step": nbytes,
                     "status_checked": True,
                     "copy_ceiling_ms": ceiling,

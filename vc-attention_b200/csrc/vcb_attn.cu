@@ -85,6 +85,7 @@ constexpr uint32_t kOffMisc = kOffBars + kNumBars * 8;
 constexpr uint32_t kSmemBytes = kOffMisc + 16;
 constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;
 constexpr uint32_t kTmemCols = 512;
+constexpr int kRegSplit = 32 * (4 * 80 + 4 * 192 + 4 * 192);   // the roles' setmaxnreg shares, per CTA
 // Tensor memory: one S buffer, and two of P (the E4M3 codes, 4 per column)
 // and O (128 channels, then 16 columns of row mass).  The D operands sit at
 // multiples of 64 columns.
@@ -93,6 +94,9 @@ constexpr uint32_t kColO0 = 128, kColO1 = 320;
 constexpr uint32_t kColP0 = 272, kColP1 = 464;
 constexpr uint32_t kColMass = 128;                // the row-mass column inside O_b
 constexpr int kPvN = 144;                         // N of the PV MMA with the row-mass columns
+static_assert(kColS + 128 <= kColO0 && kColO0 + kPvN <= kColP0 && kColP0 + 32 <= kColO1 &&
+                  kColO1 + kPvN <= kColP1 && kColP1 + 32 <= kTmemCols,
+              "S, O0, P0, O1 and P1 must not overlap in the allocated columns");
 static_assert(kStageBytes % 1024 == 0, "swizzled tiles need 1024-byte aligned stages");
 static_assert(kVRows0 + kVRows1 == 128 && kVRows1 % 8 == 0 && 2 * kVRows0 == kPvN, "V split");
 
@@ -671,8 +675,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
 template <bool M, bool P>
 int launch(const Params& p, cudaStream_t st) {
     static int max_clusters[64][8] = {};
-    return launch_pairs(attn_kernel<M, P>, p, p.items, kThreads, kSmemAlloc, max_clusters, (M ? 2 : 0) | (P ? 1 : 0),
-                        st);
+    return launch_pairs(attn_kernel<M, P>, p, p.items, kThreads, kSmemAlloc, kRegSplit, max_clusters,
+                        (M ? 2 : 0) | (P ? 1 : 0), st);
 }
 
 // Self-test of the bounded waits, with no GPU fault involved.  One CTA sets up

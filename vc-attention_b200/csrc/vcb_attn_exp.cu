@@ -67,6 +67,7 @@ constexpr uint32_t kOffMisc = kOffBars + kNumBars * 8;
 constexpr uint32_t kSmemBytes = kOffMisc + 16;
 constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;
 constexpr uint32_t kTmemCols = 512;
+constexpr int kRegSplit = 32 * (4 * 80 + 8 * 88 + 8 * 112);   // the roles' setmaxnreg shares, per CTA
 constexpr uint32_t kColS = 0;                     // S0, S1 (P and the row-mass pieces inside)
 constexpr uint32_t kColO = 256;                   // O0, O1
 constexpr uint32_t kColMass = 16;                 // row-mass operand: S_b columns [16, 24)
@@ -644,8 +645,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
 template <bool M, bool P>
 int launch(const Params& p, cudaStream_t st) {
     static int max_clusters[64][8] = {};
-    return launch_pairs(attn_kernel<M, P>, p, p.items, kThreads, kSmemAlloc, max_clusters, (M ? 2 : 0) | (P ? 1 : 0),
-                        st);
+    return launch_pairs(attn_kernel<M, P>, p, p.items, kThreads, kSmemAlloc, kRegSplit, max_clusters,
+                        (M ? 2 : 0) | (P ? 1 : 0), st);
 }
 
 }  // namespace

@@ -275,10 +275,13 @@ int make_map(CUtensorMap* map, const void* base, uint64_t width, uint64_t rows, 
 
 
 // Launches a paired kernel (clusters of 2 CTAs) with as many pairs as are
-// resident at once, looked up once per device and variant.
+// resident at once, looked up once per device and variant.  `reg_split` is
+// the sum of the roles' setmaxnreg shares (registers per CTA): a kernel
+// whose launch registers cannot hold it would wait in setmaxnreg.inc
+// forever, so that build is refused before it runs.
 template <typename Kernel, typename P>
-int launch_pairs(Kernel kernel, const P& p, int items, int threads, uint32_t smem_bytes, int (&cache)[64][8],
-                 int variant, cudaStream_t st) {
+int launch_pairs(Kernel kernel, const P& p, int items, int threads, uint32_t smem_bytes, int reg_split,
+                 int (&cache)[64][8], int variant, cudaStream_t st) {
     VCB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes));
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
@@ -296,6 +299,11 @@ int launch_pairs(Kernel kernel, const P& p, int items, int threads, uint32_t sme
     if (dev < 0 || dev >= 64) return fail(VCB_ERR_INVALID_ARGUMENT, "device ordinal %d out of range", dev);
     int& ncl_max = cache[dev][variant];
     if (ncl_max == 0) {
+        cudaFuncAttributes fa;
+        VCB_CUDA(cudaFuncGetAttributes(&fa, kernel));
+        if (fa.numRegs * threads < reg_split)
+            return fail(VCB_ERR_CUDA, "attention kernel launched with %d registers x %d threads, below its %d-register "
+                        "split", fa.numRegs, threads, reg_split);
         cfg.gridDim = dim3(2 * 148);
         int n = 0;
         VCB_CUDA(cudaOccupancyMaxActiveClusters(&n, kernel, &cfg));

@@ -85,7 +85,8 @@ constexpr uint32_t kOffMisc = kOffBars + kNumBars * 8;
 constexpr uint32_t kSmemBytes = kOffMisc + 16;
 constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;
 constexpr uint32_t kTmemCols = 512;
-constexpr int kRegSplit = 32 * (4 * 80 + 4 * 192 + 4 * 192);   // the roles' setmaxnreg shares, per CTA
+// the roles' setmaxnreg shares, per CTA (the correction's is 224 with V-Smooth)
+constexpr int reg_split(bool has_mean) { return 32 * (4 * 80 + 4 * 192 + 4 * (has_mean ? 224 : 192)); }
 // Tensor memory: one S buffer, and two of P (the E4M3 codes, 4 per column)
 // and O (128 channels, then 16 columns of row mass).  The D operands sit at
 // multiples of 64 columns.
@@ -503,20 +504,8 @@ __device__ void correction_role(const Params& p, uint8_t* smem, const Bars& B, c
 #pragma unroll
                 for (int i = 0; i < 64; ++i) acc[i] = fmul2(acc[i], aa);
             }
-            float M = 0.0f;
-#pragma unroll
-            for (int ch = 0; ch < 4; ++ch) {
-                uint32_t o[32];
-                tmem_ld32_at<0>(ob + 32 * ch, o);
-                uint32_t mraw = 0;
-                if (ch == 0) mraw = tmem_ld32_x1(ob + kColMass);
-                tmem_wait_ld();
-                if (ch == 0) M = __uint_as_float(mraw);
-                if (ch == 3) {
-                    tc_fence_before();
-                    __syncwarp();
-                    mbar_arrive_cluster_if(lead_o + 8 * b, lane == 0);
-                }
+            float M;
+            auto chunk = [&](const uint32_t (&o)[32], int ch) {
                 const float2 mm = make_float2(M, M);
 #pragma unroll
                 for (int q = 0; q < 8; ++q) {
@@ -531,6 +520,45 @@ __device__ void correction_role(const Params& p, uint8_t* smem, const Bars& B, c
                     }
                     acc[i] = ffma2(o01, make_float2(vs.x, vs.y), acc[i]);
                     acc[i + 1] = ffma2(o23, make_float2(vs.z, vs.w), acc[i + 1]);
+                }
+            };
+            if (HAS_MEAN) {
+                // V-Smooth: the next 32-column chunk of O_b loads while the
+                // current one is computed, so that only the first load's
+                // latency comes before the release of O_b, which PV_{g+2}
+                // waits for (two chunks in registers: the 224-register share)
+                uint32_t oc[2][32];
+                tmem_ld32_at<0>(ob, oc[0]);
+                M = __uint_as_float(tmem_ld32_x1(ob + kColMass));
+                tmem_wait_ld();
+                tmem_ld32_at<0>(ob + 32, oc[1]);
+                chunk(oc[0], 0);
+                tmem_wait_ld();
+                tmem_ld32_at<0>(ob + 64, oc[0]);
+                chunk(oc[1], 1);
+                tmem_wait_ld();
+                tmem_ld32_at<0>(ob + 96, oc[1]);
+                chunk(oc[0], 2);
+                tmem_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                mbar_arrive_cluster_if(lead_o + 8 * b, lane == 0);
+                chunk(oc[1], 3);
+            } else {
+#pragma unroll
+                for (int ch = 0; ch < 4; ++ch) {
+                    uint32_t o[32];
+                    tmem_ld32_at<0>(ob + 32 * ch, o);
+                    uint32_t mraw = 0;
+                    if (ch == 0) mraw = tmem_ld32_x1(ob + kColMass);
+                    tmem_wait_ld();
+                    if (ch == 0) M = __uint_as_float(mraw);
+                    if (ch == 3) {
+                        tc_fence_before();
+                        __syncwarp();
+                        mbar_arrive_cluster_if(lead_o + 8 * b, lane == 0);
+                    }
+                    chunk(o, ch);
                 }
             }
             den = __fadd_rn(__fmul_rn(alpha, den), M);
@@ -646,7 +674,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
     // role's code within its share): producer/MMA group 80 (the unrolled MMA
     // loop with its item cursor spills below 72), softmax 192 (a row's 128
     // scores and 32 code words), correction 192 (a row's 128 accumulators and
-    // one 32-column chunk of O); 10240 + 24576 + 24576 = 59392 of 64512.
+    // one 32-column chunk of O; 224 with V-Smooth, two chunks); 10240 + 24576
+    // + 24576 = 59392, or + 28672 = 63488, of 64512.
     if (warp < 4) {
         reg_dealloc<80>();
         if (warp == 0 && lane == 0) producer(p, smem, B, wait, rank, c, ncl);
@@ -657,7 +686,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
         reg_alloc<192>();
         softmax_role<PROBE>(p, smem, B, wait, tmem, rank, c, ncl, warp & 3, lane);
     } else {
-        reg_alloc<192>();
+        if (HAS_MEAN) reg_alloc<224>();
+        else reg_alloc<192>();
         correction_role<HAS_MEAN>(p, smem, B, wait, tmem, rank, c, ncl, warp & 3, lane);
     }
     tc_fence_before();
@@ -675,7 +705,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
 template <bool M, bool P>
 int launch(const Params& p, cudaStream_t st) {
     static int max_clusters[64][8] = {};
-    return launch_pairs(attn_kernel<M, P>, p, p.items, kThreads, kSmemAlloc, kRegSplit, max_clusters,
+    return launch_pairs(attn_kernel<M, P>, p, p.items, kThreads, kSmemAlloc, reg_split(M), max_clusters,
                         (M ? 2 : 0) | (P ? 1 : 0), st);
 }
 

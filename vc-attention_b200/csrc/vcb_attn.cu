@@ -30,27 +30,31 @@
 //               scores; the f16-subnormal conversion rounds to the integer
 //               code and clamps it at zero); P_g into P_b.
 //   warps 8-11  correction, one thread per row (128 channels):
-//               acc = alpha acc + (O + M mu) vscale, den = alpha den + M;
+//               acc = alpha acc + (O + M u) vscale with u = mu / vscale,
+//               den = alpha den + M;
 //               epilogue acc / den in the output dtype after each item.
 //
 // Row mass on the tensor core.  The PV MMA has N = 144: the odd CTA's B rows
 // 56..71 of every stage hold E4M3 ones, so O columns 128..143 each receive
 // sum(P) of the row, the ExpCast row mass of decoded probabilities
 // (core.py:330-332), from the same products as PV.  The softmax then only
-// encodes.  The exp mode's row mass is the FP32 sum of unrounded
-// probabilities, which the softmax keeps computing.
+// encodes.  (The exp modes, whose row mass is the FP32 sum of unrounded
+// probabilities, run on the kernel of vcb_attn_exp.cu.)
 //
-// Latency hiding: S is double-buffered in TMEM (S0, S1, then O with its mass
-// columns: 400 of 512 columns).  P_g lives in S_g's columns, so the MMA issues
-// PV_g and then QK_{g+2} into the same buffer (the tensor pipe keeps issue
-// order).  PV_g waits for the corrections' read of O_{g-1} and for K_{g+2}.
-// The commit that signals PV_g done (o_full, to both CTAs) also frees K/V
-// stage g % 8.
+// Latency hiding: TMEM holds one S buffer, two O buffers with their mass
+// columns and two compact P buffers (480 of 512 columns).  The softmax
+// releases S (s_free) as soon as its row is in registers, so QK_{g+1} runs
+// during tile g's encode.  PV_g waits for P_g, for the corrections' read of
+// O_b from tile g - 2 and for its stage; the softmax overwrites P_b only after
+// PV_{g-2} has read it.  The commit that signals PV_g done (o_full, to both
+// CTAs) lets the corrections read O_b; another frees K/V stage g % 8.  In the
+// combined mode the chain PV_g -> the corrections' read of O_b -> PV_{g+2} is
+// on the critical path, so with V-Smooth the correction prefetches O's
+// chunks and only one TMEM load latency comes before the release.
 //
 // Numerical contract (core.py:307-341): S = (q8 . k8) * qs * ks * scale;
 // ExpCast code = rne(clamp(fma(S - m, 8 log2 e, 119.65), 0, 120)) viewed as
-// E4M3 with a 1/256 scale, row mass = sum of decoded P; non-ExpCast P8 =
-// e4m3(exp(S - m) * 256) with an FP32 row mass of exp; V-mean recovery adds
+// E4M3 with a 1/256 scale, row mass = sum of decoded P; V-mean recovery adds
 // rowmass * mu / vscale to PV before the scale and is rescaled with the
 // running max.  The accumulators are kept in units of 256 (acc256 = 256 acc,
 // den256 = 256 den); 256 is a power of two, so no rounding changes.  Every

@@ -81,10 +81,10 @@ constexpr uint32_t kOffQ = 0;                     // Q buffers 0, 1
 constexpr uint32_t kOffStages = 2 * kQBytes;
 constexpr uint32_t kMetaBytes = 1024;             // vscale[128], stored mean mu / vscale [128]
 constexpr uint32_t kOffMeta = kOffStages + kStages * kStageBytes;
-constexpr int kStatSlots = 8;                     // per-tile alpha ring
+constexpr int kStatSlots = kMetaSlots;            // per-tile alpha ring, as deep as the meta ring
 constexpr uint32_t kOffStats = kOffMeta + kMetaSlots * kMetaBytes;  // alpha[8][128]
 constexpr uint32_t kOffBars = kOffStats + kStatSlots * 128 * 4;
-constexpr int kNumBars = 2 + 2 + 2 * kStages + 2 * kMetaSlots + 5 * 2 + 2 * kStatSlots + 2;
+constexpr int kNumBars = 2 + 2 + 2 * kStages + 2 * kMetaSlots + 5 * 2 + kStatSlots + 2;
 constexpr uint32_t kOffMisc = kOffBars + kNumBars * 8;
 constexpr uint32_t kSmemBytes = kOffMisc + 16;
 constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;
@@ -131,14 +131,13 @@ struct Bars {
     uint64_t* kv_full;     // [kStages]  even CTA: both halves of K / V (/ mean operand) landed
     uint64_t* kv_empty;    // [kStages]  both: the PV of the stage's tile is done
     uint64_t* meta_full;   // [kMetaSlots]
-    uint64_t* meta_empty;  // [kMetaSlots]  the 8 correction warps have read the slot
+    uint64_t* meta_empty;  // [kMetaSlots]  the correction warps have read the tile's meta and alpha slots
     uint64_t* s_full;      // [1]  both: QK_g done
     uint64_t* s_free;      // [1]  even CTA: the softmax of all 256 rows has read S_g
     uint64_t* p_full;      // [2]  even CTA: P_g of all 256 rows in P_b, b = g % 2
     uint64_t* o_full;      // [2]  both: PV_g done, for the tiles g of parity b
     uint64_t* o_free;      // [2]  even CTA: both corrections have read O for a tile of parity b
-    uint64_t* st_full;     // [kStatSlots]  alpha of tile g
-    uint64_t* st_free;     // [kStatSlots]
+    uint64_t* st_full;     // [kStatSlots]  alpha of tile g (freed by meta_empty: one release per tile)
     uint64_t* drain;       // [2]  one per MMA thread
 };
 
@@ -157,7 +156,6 @@ __device__ __forceinline__ Bars bars_at(uint8_t* smem) {
     r.o_full = b; b += 2;
     r.o_free = b; b += 2;
     r.st_full = b; b += kStatSlots;
-    r.st_free = b; b += kStatSlots;
     r.drain = b;
     return r;
 }
@@ -381,7 +379,7 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, const Bars& B, cons
             // slot this tile writes at its end and the completion of PV_{g-2},
             // the last reader of the P buffer this tile writes
             if (!wait.all(&B.s_full[0], g & 1,
-                          g >= (uint32_t)kStatSlots ? &B.st_free[slot] : nullptr, ((g / kStatSlots) - 1) & 1,
+                          g >= (uint32_t)kStatSlots ? &B.meta_empty[slot] : nullptr, ((g / kStatSlots) - 1) & 1,
                           g >= 2 ? &B.o_full[b] : nullptr, ((g - 2) >> 1) & 1))
                 return;
             tc_fence_after();
@@ -497,8 +495,6 @@ __device__ void correction_role(const Params& p, uint8_t* smem, const Bars& B, c
                 return;
             tc_fence_after();
             const float alpha = st_alpha[slot * 128 + row];
-            __syncwarp();
-            mbar_arrive_if(&B.st_free[slot], lane == 0);
             const float4* vsp = reinterpret_cast<const float4*>(smem + kOffMeta + s * kMetaBytes);
             const float4* usp = vsp + 32;                          // the stored means follow the scales
             const bool rescale = __any_sync(0xffffffffu, alpha != 1.0f);
@@ -646,7 +642,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
         }
         for (int s = 0; s < kStatSlots; ++s) {
             mbar_init(&B.st_full[s], 4);
-            mbar_init(&B.st_free[s], 4);
         }
         *abort = 0;
         fence_barrier_init();

@@ -112,3 +112,50 @@ def test_layout_requires_request_id_and_valid_steps(cpu_grouping):
         cache.layout(v, step=0, total_steps=4, request_id=None, layer_id=0)
     with pytest.raises(ValueError, match="step"):
         cache.layout(v, step=4, total_steps=4, request_id="r", layer_id=0)
+
+
+def test_peek_predicts_layout_without_changing_the_cache(cpu_grouping):
+    """LayoutCache.peek gives layout()'s decision for the same call (active,
+    refresh, and the cached pi exactly when it would be reused) over the
+    recorded schedule script, including the reversed step, the new request and
+    the changed shape, and clusters nothing and changes nothing itself."""
+    cache = LayoutCache(Config(v_smooth=True))
+    base_v = cases.clustered_values(tokens=64, heads=1, dim=8)
+    reused = 0
+    for request, step, total, trim in cases.schedule_script():
+        v = base_v[:, :, : base_v.shape[2] - trim]
+        calls, rid, states = len(cpu_grouping), cache._request_id, dict(cache._states)
+        fields = {k: dict(s) for k, s in states.items()}
+        pi_p, active_p, refresh_p = cache.peek(v, step=step, total_steps=total, request_id=request, layer_id=0)
+        assert len(cpu_grouping) == calls and cache._request_id == rid and cache._states == states
+        assert all(dict(cache._states[k]) == f for k, f in fields.items())
+        pi, active, refresh = cache.layout(v, step=step, total_steps=total, request_id=request, layer_id=0)
+        assert (active_p, refresh_p) == (active, refresh), (request, step)
+        if active and not refresh:
+            assert pi_p is pi
+            reused += 1
+        else:
+            assert pi_p is None
+    assert reused > 0
+    with pytest.raises(ValueError, match="request_id"):
+        cache.peek(base_v, step=0, total_steps=1, request_id=None, layer_id=0)
+    with pytest.raises(ValueError, match="step"):
+        cache.peek(base_v, step=3, total_steps=3, request_id="a", layer_id=0)
+
+
+def test_kv_order_must_be_known():
+    q, k, v = cases.reference_test_inputs((1, 2, 19, 35, 16, 16))
+    with pytest.raises(ValueError, match="kv_order"):
+        attention(q, k, v, Config(), kv_order="sorted")
+
+
+def test_to_layout_order_gathers_rows_through_pi():
+    x = torch.arange(2 * 3 * 5 * 4, dtype=torch.float32).reshape(2, 3, 5, 4)
+    pi = torch.stack([torch.randperm(5, generator=torch.Generator().manual_seed(i)) for i in range(6)])
+    pi = pi.reshape(2, 3, 5).to(torch.int32)
+    from vc_attention_b200 import to_layout_order
+    y = to_layout_order(x, pi)
+    for b in range(2):
+        for h in range(3):
+            for r in range(5):
+                assert torch.equal(y[b, h, r], x[b, h, int(pi[b, h, r])])

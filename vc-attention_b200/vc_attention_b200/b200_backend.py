@@ -167,10 +167,13 @@ def raise_for_status(status):
 
 
 @torch.no_grad()
-def _attention(q, k, v, cfg, *, cache, step, total_steps, request_id, layer_id, scale, status=None):
+def _attention(q, k, v, cfg, *, cache, step, total_steps, request_id, layer_id, scale, status=None,
+               kv_order="natural"):
     """cuda_backend._attention (cuda_backend.py:26-66) for sm_100a.  With a
     caller-owned ``status`` word the call does not wait for the device; the
-    caller reads the word later (raise_for_status) and owns the cache rollback."""
+    caller reads the word later (raise_for_status) and owns the cache rollback.
+    With ``kv_order="layout"`` K and V are already in the cached layout's
+    order and are read without the gather of cuda_backend.py:49-51."""
     from .core import LayoutCache
 
     _require_b200(q)
@@ -186,14 +189,19 @@ def _attention(q, k, v, cfg, *, cache, step, total_steps, request_id, layer_id, 
         raise ValueError("cache.config must match config")
     if status is not None and (status.device != q.device or status.dtype != torch.int32 or status.numel() != 1):
         raise ValueError("status must be a one-element int32 tensor on the inputs' device")
+    if kv_order == "layout":
+        cached, _, _ = cache.peek(v, step=step, total_steps=total_steps, request_id=request_id, layer_id=layer_id)
+        if cached is None:
+            raise ValueError('kv_order="layout" needs a step that reuses a cached layout '
+                             "(LayoutCache.peek returns its pi)")
     snapshot = cache._snapshot(layer_id)
     with torch.cuda.device(q.device):
         pi, active, refreshed = cache.layout(v, step=step, total_steps=total_steps, request_id=request_id,
                                              layer_id=layer_id)
         qc, kc, vc = q.contiguous(), k.contiguous(), v.contiguous()
         try:
-            output = forward(qc, kc, vc, cfg, pi=pi, active=active, scale=scale, status=status,
-                             check_status=status is None)
+            output = forward(qc, kc, vc, cfg, pi=pi if kv_order == "natural" else None, active=active,
+                             scale=scale, status=status, check_status=status is None)
         except (ValueError, RuntimeError):
             cache._restore(snapshot, layer_id)
             raise

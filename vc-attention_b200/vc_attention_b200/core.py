@@ -145,6 +145,39 @@ class LayoutCache:
             _mark_use(state["pi"])
         return (None if state is None else state["pi"]), active, refresh
 
+    def peek(self, v, *, step, total_steps, request_id, layer_id):
+        """What ``layout`` would decide for this call, without changing the
+        cache or clustering anything: ``(pi, active, refresh)``, where ``pi`` is
+        the cached permutation when the call would reuse it (active and no
+        refresh) and None otherwise.  ``v`` is V or any tensor with V's shape,
+        device and dtype.
+
+        The reference gathers K and V through ``pi`` on every call
+        (cuda_backend.py:49-51).  A producer that keeps K and V in layout order
+        (for example by writing the QKV projection's rows through ``pi``) asks
+        here before it writes them, and passes ``kv_order="layout"`` to
+        ``attention`` when ``pi`` is not None; the forward then skips the
+        gather."""
+        if request_id is None:
+            raise ValueError("A persistent layout cache requires request_id")
+        if total_steps < 1 or not 0 <= step < total_steps:
+            raise ValueError("Invalid denoising step/total_steps")
+        state = self._states.get(layer_id) if request_id == self._request_id else None
+        signature = (tuple(v.shape), str(v.device), v.dtype, total_steps)
+        if state is not None and (state["signature"] != signature or step < state["step"]):
+            state = None
+        active = self.config.v_smooth and step < math.ceil(total_steps * self.config.active_fraction)
+        refresh = active and (state is None or step - state["refresh_step"] >= self.config.refresh_interval)
+        reuse = active and not refresh and state is not None
+        return (state["pi"] if reuse else None), active, refresh
+
+
+def to_layout_order(x, pi):
+    """Rows of ``x`` [B, H, S, D] in layout order: row r of the result is row
+    ``pi[b, h, r]`` of ``x`` (the gather of cuda_backend.py:49-51).  For
+    producers without a fused epilogue, and for tests."""
+    return x.gather(-2, pi.long().unsqueeze(-1).expand_as(x))
+
 
 def _validate(q, k, v, causal, mask):
     """core.py:214-232.  Finiteness is checked on the device by the kernels
@@ -184,6 +217,7 @@ def attention(
     causal=False,
     mask=None,
     status=None,
+    kv_order="natural",
 ):
     """Return (output, counters) as core.attention does (core.py:243-351).
 
@@ -198,11 +232,22 @@ def attention(
     flags must be kept apart); the caller later calls
     ``b200_backend.raise_for_status(status)``
     and, if it raises, ``counters["rollback"]()`` to put the layout cache
-    back as it was before this call."""
+    back as it was before this call.
+
+    ``kv_order`` (also an addition, default "natural") set to "layout" says
+    that K and V already come in the cached layout's order: row r is token
+    ``pi[r]`` of the call's sequence, with ``pi`` as ``cache.peek`` returns it
+    for this step.  The forward then reads them as they are instead of
+    gathering them.  It is valid only on a step that reuses a cached layout;
+    on any other step the call raises ValueError and leaves the cache as it
+    was.  The output rows follow Q, whose order never changes."""
     cfg = config or Config()
     _validate(q, k, v, causal, mask)
+    if kv_order not in ("natural", "layout"):
+        raise ValueError('kv_order must be "natural" or "layout"')
     from .b200_backend import _attention
 
     return _attention(q, k, v, cfg, cache=cache, step=step, total_steps=total_steps,
                       request_id=request_id, layer_id=layer_id,
-                      scale=q.shape[-1] ** -0.5 if scale is None else scale, status=status)
+                      scale=q.shape[-1] ** -0.5 if scale is None else scale, status=status,
+                      kv_order=kv_order)

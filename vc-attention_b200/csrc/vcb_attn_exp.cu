@@ -562,6 +562,7 @@ __device__ void correction_role(const Params& p, uint8_t* smem, const Bars& B, c
 
 template <bool HAS_MEAN, bool PROBE>
 __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant__ Params p) {
+    pdl_wait();
     // The swizzled TMA/MMA layouts need a 1024-byte aligned base; the kernel
     // declares no static shared memory, so the dynamic window starts aligned.
     // Checked anyway: a misaligned window reports an error and does nothing

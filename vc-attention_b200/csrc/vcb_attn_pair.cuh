@@ -284,16 +284,18 @@ int launch_pairs(Kernel kernel, const P& p, int items, int threads, uint32_t sme
                  int (&cache)[64][8], int variant, cudaStream_t st) {
     VCB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes));
     cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;   // the kernel begins with pdl_wait()
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.blockDim = dim3(threads);
     cfg.dynamicSmemBytes = smem_bytes;
     cfg.stream = st;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 1;          // the occupancy query takes the cluster shape alone
     int dev = 0;
     VCB_CUDA(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) return fail(VCB_ERR_INVALID_ARGUMENT, "device ordinal %d out of range", dev);
@@ -312,6 +314,7 @@ int launch_pairs(Kernel kernel, const P& p, int items, int threads, uint32_t sme
     }
     const int ncl = items < ncl_max ? items : ncl_max;
     cfg.gridDim = dim3(2 * ncl);
+    cfg.numAttrs = 2;
     VCB_CUDA(cudaLaunchKernelEx(&cfg, kernel, p));
     return VCB_OK;
 }

@@ -42,6 +42,8 @@ __device__ __forceinline__ float to_float(__nv_bfloat16 x) { return __bfloat162f
 
 template <typename T>
 __global__ void cluster_init_kernel(ClusterArgs a, const float* __restrict__ centers_in, InitIdx init) {
+    pdl_wait();
+    pdl_open();
     const int64_t h = blockIdx.x;
     for (int i = threadIdx.x; i < a.count * a.D; i += blockDim.x) {
         const int c = i / a.D, d = i % a.D;
@@ -54,6 +56,8 @@ __global__ void cluster_init_kernel(ClusterArgs a, const float* __restrict__ cen
 
 template <typename T>
 __global__ void __launch_bounds__(256) cluster_assign_kernel(ClusterArgs a) {
+    pdl_wait();
+    pdl_open();
     __shared__ __align__(16) float cen[kMaxClusters * 128];
     __shared__ float cnorm[kMaxClusters];
     __shared__ uint8_t lab[kChunk];
@@ -192,6 +196,8 @@ __global__ void __launch_bounds__(256) cluster_assign_kernel(ClusterArgs a) {
 //              sums added in order by thread (cluster, d).
 template <typename T>
 __global__ void __launch_bounds__(256, 2) cluster_assign128_kernel(ClusterArgs a) {
+    pdl_wait();
+    pdl_open();
     constexpr int RB = 128 * (int)sizeof(T);        // bytes per staged row
     constexpr int NCH = RB / 16;                    // 16-byte chunks per row
     constexpr int E = 16 / (int)sizeof(T);          // elements per chunk
@@ -371,6 +377,8 @@ __global__ void __launch_bounds__(256, 2) cluster_assign128_kernel(ClusterArgs a
 // One CTA per (head, cluster), thread d per channel; chunks added in order
 // (the loads are independent, only the adds are chained).
 __global__ void __launch_bounds__(128) cluster_update_kernel(ClusterArgs a) {
+    pdl_wait();
+    pdl_open();
     const int64_t h = blockIdx.x;
     const int c = blockIdx.y, d = threadIdx.x;
     if (d >= a.D) return;
@@ -391,6 +399,8 @@ __global__ void __launch_bounds__(128) cluster_update_kernel(ClusterArgs a) {
 // chunk-minor order: one CTA per head, each thread a contiguous run of that
 // order, the run totals scanned across warps (integer sums: any order).
 __global__ void __launch_bounds__(256) cluster_offsets_kernel(ClusterArgs a) {
+    pdl_wait();
+    pdl_open();
     __shared__ int wsum[8];
     const int64_t h = blockIdx.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -422,6 +432,8 @@ __global__ void __launch_bounds__(256) cluster_offsets_kernel(ClusterArgs a) {
 // earlier tokens of its cluster = rank inside its warp (match mask) plus the
 // counts of the warps before it.
 __global__ void __launch_bounds__(256) cluster_scatter_kernel(ClusterArgs a) {
+    pdl_wait();
+    pdl_open();
     __shared__ int wcnt[8][kMaxClusters];
     const int64_t h = blockIdx.y;
     const int chunk = blockIdx.x;
@@ -474,8 +486,8 @@ int run(const vcb_group_args* p, cudaStream_t st) {
     a.off = reinterpret_cast<int32_t*>(take((size_t)p->heads * nchunk * count * sizeof(int32_t)));
     InitIdx init{};
     linspace_indices(p->s, count, init.idx);
-    cluster_init_kernel<T><<<(unsigned)p->heads, 256, 0, st>>>(a, p->centers_in, init);
-    VCB_CUDA(cudaGetLastError());
+    VCB_CUDA(launch_pdl(cluster_init_kernel<T>, dim3((unsigned)p->heads), dim3(256), 0, st, a, p->centers_in,
+                        init));
     const size_t fast_smem = (size_t)kChunk * 128 * sizeof(T) + 8 * 8 * 128 * sizeof(float) +
                              (size_t)((count + 3) / 4) * 128 * 8 * sizeof(float);
     if (p->d == 128)
@@ -483,17 +495,14 @@ int run(const vcb_group_args* p, cudaStream_t st) {
                                       (int)fast_smem));
     for (int it = 0; it < p->iterations; ++it) {
         if (p->d == 128)
-            cluster_assign128_kernel<T><<<dim3(nchunk, (unsigned)p->heads), 256, fast_smem, st>>>(a);
+            VCB_CUDA(launch_pdl(cluster_assign128_kernel<T>, dim3(nchunk, (unsigned)p->heads), dim3(256), fast_smem,
+                                st, a));
         else
-            cluster_assign_kernel<T><<<dim3(nchunk, (unsigned)p->heads), 256, 0, st>>>(a);
-        VCB_CUDA(cudaGetLastError());
-        cluster_update_kernel<<<dim3((unsigned)p->heads, (unsigned)count), 128, 0, st>>>(a);
-        VCB_CUDA(cudaGetLastError());
+            VCB_CUDA(launch_pdl(cluster_assign_kernel<T>, dim3(nchunk, (unsigned)p->heads), dim3(256), 0, st, a));
+        VCB_CUDA(launch_pdl(cluster_update_kernel, dim3((unsigned)p->heads, (unsigned)count), dim3(128), 0, st, a));
     }
-    cluster_offsets_kernel<<<(unsigned)p->heads, 256, 0, st>>>(a);
-    VCB_CUDA(cudaGetLastError());
-    cluster_scatter_kernel<<<dim3(nchunk, (unsigned)p->heads), 256, 0, st>>>(a);
-    VCB_CUDA(cudaGetLastError());
+    VCB_CUDA(launch_pdl(cluster_offsets_kernel, dim3((unsigned)p->heads), dim3(256), 0, st, a));
+    VCB_CUDA(launch_pdl(cluster_scatter_kernel, dim3(nchunk, (unsigned)p->heads), dim3(256), 0, st, a));
     return VCB_OK;
 }
 

@@ -297,6 +297,33 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
     return d;
 }
 
+// Programmatic dependent launch.  Every kernel of the forward begins with
+// pdl_wait(), which returns once the stream's previous grid has completed and
+// its writes are visible (at once for a grid launched without the attribute),
+// so no read or write of a grid runs ahead of its producer.  pdl_open() lets
+// the next grid's CTAs become resident during this grid's last wave; they
+// then wait in their own pdl_wait().
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_open() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// kernel<<<grid, block, smem, st>>>(args...) with programmatic stream
+// serialisation, so that the grid may launch before its predecessor ends.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 template <uint32_t N> __device__ __forceinline__ void reg_alloc() {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
 }

@@ -19,6 +19,8 @@ constexpr int kKsumLanes = 16;
 template <typename T>
 __global__ void __launch_bounds__(256) k_colsum_kernel(const T* __restrict__ k, int64_t S, int D,
                                                        float* __restrict__ partial, int nchunk) {
+    pdl_wait();
+    pdl_open();
     __shared__ float part[kKsumLanes][128];
     const int64_t h = blockIdx.y;
     const int chunk = blockIdx.x;
@@ -58,6 +60,8 @@ __global__ void __launch_bounds__(256) k_colsum_kernel(const T* __restrict__ k, 
 
 __global__ void k_mean_kernel(const float* __restrict__ partial, int nchunk, int64_t S,
                               float* __restrict__ mean) {
+    pdl_wait();
+    pdl_open();
     const int64_t h = blockIdx.x;
     const int c = threadIdx.x;
     float total = 0.0f;
@@ -306,6 +310,8 @@ __device__ __forceinline__ void encode_half128(const float2 (&x)[32], float pre,
 // FIX: D == 128 with the 128-point Hadamard, on the packed helpers.
 template <typename T, bool FIX>
 __global__ void __launch_bounds__(512) qk_quant_kernel(RowArgs a) {
+    pdl_wait();
+    pdl_open();
     __shared__ __align__(16) float smean[128];
     __shared__ int32_t stok[256];
     __shared__ float red[16];
@@ -445,6 +451,8 @@ __device__ __forceinline__ void lds8x2(uint32_t addr, float2* o) {
 template <typename T>
 __global__ void __launch_bounds__(kStagedThreads, 1) qk_quant_staged_kernel(RowArgs a, int64_t slabs_per_head,
                                                                             int64_t nslabs) {
+    pdl_wait();
+    pdl_open();
     extern __shared__ __align__(128) uint8_t sm[];
     float* partial = reinterpret_cast<float*>(sm + kSlabStages * kSlabStageBytes);   // [2][kStagedWarps]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -526,6 +534,8 @@ __global__ void __launch_bounds__(kStagedThreads, 1) qk_quant_staged_kernel(RowA
 // Transform-only rows (the preprocess_qk export): one row per thread.
 template <typename T>
 __global__ void __launch_bounds__(128) qk_transform_kernel(RowArgs a) {
+    pdl_wait();
+    pdl_open();
     __shared__ float smean[128];
     const int64_t h = blockIdx.y;
     if (a.mean) smean[threadIdx.x] = a.mean[h * 128 + threadIdx.x];
@@ -554,11 +564,9 @@ template <typename T>
 int launch_k_mean(const void* k, int64_t heads, int64_t S, int D, float* partial, float* mean,
                   cudaStream_t st) {
     const int nchunk = (int)((S + kKsumChunk - 1) / kKsumChunk);
-    k_colsum_kernel<T><<<dim3(nchunk, (unsigned)heads), 256, 0, st>>>(static_cast<const T*>(k), S, D,
-                                                                       partial, nchunk);
-    VCB_CUDA(cudaGetLastError());
-    k_mean_kernel<<<(unsigned)heads, 128, 0, st>>>(partial, nchunk, S, mean);
-    VCB_CUDA(cudaGetLastError());
+    VCB_CUDA(launch_pdl(k_colsum_kernel<T>, dim3(nchunk, (unsigned)heads), dim3(256), 0, st,
+                        static_cast<const T*>(k), S, D, partial, nchunk));
+    VCB_CUDA(launch_pdl(k_mean_kernel, dim3((unsigned)heads), dim3(128), 0, st, partial, nchunk, S, mean));
     return VCB_OK;
 }
 
@@ -573,8 +581,8 @@ int launch_rows(const RowArgs& a, int64_t heads, bool quantise, cudaStream_t st)
         const int64_t grid = nslabs < sm_count() ? nslabs : sm_count();
         auto kernel = qk_quant_staged_kernel<T>;
         VCB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kStagedSmem));
-        kernel<<<(unsigned)grid, kStagedThreads, kStagedSmem, st>>>(a, slabs_per_head, nslabs);
-        VCB_CUDA(cudaGetLastError());
+        VCB_CUDA(launch_pdl(kernel, dim3((unsigned)grid), dim3(kStagedThreads), kStagedSmem, st, a, slabs_per_head,
+                            nslabs));
         return VCB_OK;
     }
     if (quantise) {
@@ -582,13 +590,13 @@ int launch_rows(const RowArgs& a, int64_t heads, bool quantise, cudaStream_t st)
         const int rows = a.block < 256 ? a.block : 256;
         const int nthr = (rows + 15) / 16 * 32;      // two threads per row, whole warps
         if (a.D == 128 && a.hadamard)
-            qk_quant_kernel<T, true><<<dim3(grid, (unsigned)heads), nthr, 0, st>>>(a);
+            VCB_CUDA(launch_pdl(qk_quant_kernel<T, true>, dim3(grid, (unsigned)heads), dim3(nthr), 0, st, a));
         else
-            qk_quant_kernel<T, false><<<dim3(grid, (unsigned)heads), nthr, 0, st>>>(a);
+            VCB_CUDA(launch_pdl(qk_quant_kernel<T, false>, dim3(grid, (unsigned)heads), dim3(nthr), 0, st, a));
     } else {
-        qk_transform_kernel<T><<<dim3((unsigned)((a.S + 127) / 128), (unsigned)heads), 128, 0, st>>>(a);
+        VCB_CUDA(launch_pdl(qk_transform_kernel<T>, dim3((unsigned)((a.S + 127) / 128), (unsigned)heads), dim3(128), 0,
+                            st, a));
     }
-    VCB_CUDA(cudaGetLastError());
     return VCB_OK;
 }
 

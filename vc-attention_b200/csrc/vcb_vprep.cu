@@ -39,6 +39,8 @@ __global__ void __launch_bounds__(128) vprep_kernel(const T* __restrict__ v, int
                                                     int mean_type, int T_tiles, uint8_t* __restrict__ v8,
                                                     float* __restrict__ meta, uint16_t* __restrict__ mop,
                                                     int32_t* status) {
+    pdl_wait();
+    pdl_open();
     extern __shared__ __align__(16) uint8_t tile_raw[];
     T* tile = reinterpret_cast<T*>(tile_raw);     // [kTile][128] in the input type
     const int64_t h = blockIdx.y;
@@ -191,10 +193,9 @@ int launch(const vcb_v_args* p, cudaStream_t st) {
     const int T_tiles = (int)((p->s + kTile - 1) / kTile);
     const size_t smem = kTile * 128 * sizeof(T);
     VCB_CUDA(cudaFuncSetAttribute(vprep_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    vprep_kernel<T><<<dim3(T_tiles, (unsigned)p->heads), 128, smem, st>>>(
-        static_cast<const T*>(p->v), p->s, p->dv, p->pi, p->active, p->mean_type, T_tiles, p->v8,
-        p->v_meta, p->active ? p->v_mean_op : nullptr, p->status);
-    VCB_CUDA(cudaGetLastError());
+    VCB_CUDA(launch_pdl(vprep_kernel<T>, dim3(T_tiles, (unsigned)p->heads), dim3(128), smem, st,
+                        static_cast<const T*>(p->v), p->s, p->dv, p->pi, p->active, p->mean_type, T_tiles, p->v8,
+                        p->v_meta, p->active ? p->v_mean_op : nullptr, p->status));
     return VCB_OK;
 }
 }  // namespace

@@ -19,6 +19,10 @@ namespace vcb {
 constexpr int kChunk = 256;
 constexpr int kSub = 32;
 constexpr int kMaxClusters = 32;
+// clusters whose sub-chunk sums the 128-channel assign pass reduces per round:
+// 8 warps x 2 x 128 floats fit in the centres' 8 KB (8 clusters), so that the
+// pass takes ~75 KB of shared memory and three CTAs fit on an SM
+constexpr int kSumGroup = 2;
 
 struct ClusterArgs {
     const void* v;
@@ -195,7 +199,7 @@ __global__ void __launch_bounds__(256) cluster_assign_kernel(ClusterArgs a) {
 //              cluster's tokens, added lowest first (token order); sub-chunk
 //              sums added in order by thread (cluster, d).
 template <typename T>
-__global__ void __launch_bounds__(256, 2) cluster_assign128_kernel(ClusterArgs a) {
+__global__ void __launch_bounds__(256, 3) cluster_assign128_kernel(ClusterArgs a) {
     pdl_wait();
     pdl_open();
     constexpr int RB = 128 * (int)sizeof(T);        // bytes per staged row
@@ -203,9 +207,11 @@ __global__ void __launch_bounds__(256, 2) cluster_assign128_kernel(ClusterArgs a
     constexpr int E = 16 / (int)sizeof(T);          // elements per chunk
     extern __shared__ __align__(16) uint8_t dsm[];
     uint8_t* xs = dsm;                                               // [256][RB], swizzled
-    float* subs = reinterpret_cast<float*>(dsm + kChunk * RB);        // [8 warps][8 clusters][128]
     // centres twice over for packed FMAs over two tokens: [c / 4][d][c % 4][2]
-    float* cen2 = subs + 8 * 8 * 128;
+    float* cen2 = reinterpret_cast<float*>(dsm + kChunk * RB);
+    // the sub-chunk sums [8 warps][kSumGroup clusters][128] reuse the centres'
+    // space: they are first written two barriers after the last distance
+    float* subs = cen2;
     __shared__ float cnorm[kMaxClusters];
     __shared__ float hbest[2][kChunk];
     __shared__ uint8_t hidx[2][kChunk];
@@ -325,17 +331,17 @@ __global__ void __launch_bounds__(256, 2) cluster_assign128_kernel(ClusterArgs a
 
     float* ps = a.psum + ((int64_t)h * a.nchunk + chunk) * count * 128;
     const int t0 = warp * kSub, t1 = min(t0 + kSub, nvalid);
-    for (int cg = 0; cg < count; cg += 8) {
-        float s[8][4];
+    for (int cg = 0; cg < count; cg += kSumGroup) {
+        float s[kSumGroup][4];
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
+        for (int i = 0; i < kSumGroup; ++i)
 #pragma unroll
             for (int e = 0; e < 4; ++e) s[i][e] = 0.0f;
         // each cluster of the group takes its tokens of the sub-chunk in token
         // order (lowest set bit first), the order of the per-token loop
         const int mine = t0 + lane < t1 ? lab[t0 + lane] - cg : -1;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < kSumGroup; ++i) {
             unsigned m = __ballot_sync(0xffffffffu, mine == i);
             while (m) {
                 const int t = t0 + __ffs(m) - 1;
@@ -357,16 +363,16 @@ __global__ void __launch_bounds__(256, 2) cluster_assign128_kernel(ClusterArgs a
             }
         }
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-            *reinterpret_cast<float4*>(&subs[(warp * 8 + i) * 128 + 4 * lane]) =
+        for (int i = 0; i < kSumGroup; ++i)
+            *reinterpret_cast<float4*>(&subs[(warp * kSumGroup + i) * 128 + 4 * lane]) =
                 make_float4(s[i][0], s[i][1], s[i][2], s[i][3]);
         __syncthreads();
-        for (int idx = tid; idx < 8 * 128; idx += 256) {
+        for (int idx = tid; idx < kSumGroup * 128; idx += 256) {
             const int i = idx >> 7, d = idx & 127;
             if (cg + i >= count) continue;
             float part = 0.0f;
 #pragma unroll
-            for (int w = 0; w < 8; ++w) part += subs[(w * 8 + i) * 128 + d];
+            for (int w = 0; w < 8; ++w) part += subs[(w * kSumGroup + i) * 128 + d];
             ps[(cg + i) * 128 + d] = part;
         }
         __syncthreads();
@@ -488,11 +494,15 @@ int run(const vcb_group_args* p, cudaStream_t st) {
     linspace_indices(p->s, count, init.idx);
     VCB_CUDA(launch_pdl(cluster_init_kernel<T>, dim3((unsigned)p->heads), dim3(256), 0, st, a, p->centers_in,
                         init));
-    const size_t fast_smem = (size_t)kChunk * 128 * sizeof(T) + 8 * 8 * 128 * sizeof(float) +
-                             (size_t)((count + 3) / 4) * 128 * 8 * sizeof(float);
-    if (p->d == 128)
+    const size_t cen2_bytes = (size_t)((count + 3) / 4) * 128 * 8 * sizeof(float);
+    const size_t subs_bytes = (size_t)8 * kSumGroup * 128 * sizeof(float);
+    const size_t fast_smem = (size_t)kChunk * 128 * sizeof(T) + (cen2_bytes > subs_bytes ? cen2_bytes : subs_bytes);
+    if (p->d == 128) {
         VCB_CUDA(cudaFuncSetAttribute(cluster_assign128_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       (int)fast_smem));
+        VCB_CUDA(cudaFuncSetAttribute(cluster_assign128_kernel<T>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                      (int)cudaSharedmemCarveoutMaxShared));
+    }
     for (int it = 0; it < p->iterations; ++it) {
         if (p->d == 128)
             VCB_CUDA(launch_pdl(cluster_assign128_kernel<T>, dim3(nchunk, (unsigned)p->heads), dim3(256), fast_smem,

@@ -10,6 +10,13 @@
  * current PyTorch stream the same way); nothing synchronises the device,
  * and only vcb_read_status waits for the caller's stream.
  *
+ * The kernels are launched with programmatic stream serialisation, and each
+ * waits for the stream's previous grid (griddepcontrol.wait) before it reads
+ * or writes anything.  Work the caller queues after a call is ordered as
+ * usual, except a kernel of the caller's own launched with that attribute:
+ * like any dependent grid, it must wait (griddepcontrol.wait or
+ * cudaGridDependencySynchronize) before it reads the call's outputs.
+ *
  * Tensors are contiguous, batch and heads flattened: [heads, tokens, dim].
  * Functions return VCB_OK or a VCB_ERR_* code; vcb_last_error() gives the
  * message of the last failure on the calling thread.
